@@ -1,0 +1,213 @@
+/*
+ * tecoops.h — C API of the B200 (sm_100a) implementation of the Teco-Ops
+ * paged-KV attention path.
+ *
+ * Drop-in for the reference header teco/interface/include/tecoops.h:
+ * same enums (values included), same handle / tensor-descriptor API and the
+ * same signatures for the two hot-path operators.  The only type change is
+ * the stream: the reference's `sdaaStream_t` is a CUDA stream here; a typedef
+ * keeps sources that spell `sdaaStream_t` compiling.
+ *
+ * All data pointers are caller-owned DEVICE memory.  Every operator call is
+ * asynchronous on the handle's stream and never synchronises the host.
+ *
+ * Symbols of the reference's other operators (rms_norm, causal_conv1d, ...)
+ * are exported so that a program linking the reference library still links,
+ * but they return TECOOPS_STATUS_NOT_SUPPORTED (they are not on this path).
+ */
+#ifndef TECOOPS_B200_INCLUDE_TECOOPS_H_
+#define TECOOPS_B200_INCLUDE_TECOOPS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* CUDA stream handle without dragging in the CUDA headers (identical to the
+ * runtime's own definition of cudaStream_t). */
+#ifndef __CUDA_RUNTIME_API_H__
+struct CUstream_st;
+typedef struct CUstream_st *cudaStream_t;
+#endif
+typedef cudaStream_t sdaaStream_t; /* source compatibility with the reference */
+
+#define TECOOPS_DIM_MAX 8
+
+/* reference: teco/interface/include/tecoops.h:39-47 */
+typedef enum {
+    TECOOPS_STATUS_SUCCESS = 0,
+    TECOOPS_STATUS_NOT_INITIALIZED = 1,
+    TECOOPS_STATUS_ALLOC_FAILED = 2,
+    TECOOPS_STATUS_BAD_PARAM = 3,
+    TECOOPS_STATUS_INTERNAL_ERROR = 4,
+    TECOOPS_STATUS_INVALID_VALUE = 5,
+    TECOOPS_STATUS_NOT_SUPPORTED = 6,
+} tecoopsStatus_t;
+
+/* reference: tecoops.h:49-58 */
+typedef enum {
+    TECOOPS_TENSOR_NCHW = 0,
+    TECOOPS_TENSOR_NHWC = 1,
+    TECOOPS_TENSOR_CHWN = 2,
+    TECOOPS_TENSOR_NWHC = 3,
+    TECOOPS_TENSOR_NCDHW = 4,
+    TECOOPS_TENSOR_NDHWC = 5,
+    TECOOPS_TENSOR_CDHWN = 6,
+} tecoopsTensorFormat_t;
+
+/* reference: tecoops.h:60-71 */
+typedef enum {
+    TECOOPS_ALGO_0 = 0,
+    TECOOPS_ALGO_1,
+    TECOOPS_ALGO_2,
+    TECOOPS_ALGO_3,
+    TECOOPS_ALGO_4,
+    TECOOPS_ALGO_5,
+    TECOOPS_ALGO_6,
+    TECOOPS_ALGO_7,
+    TECOOPS_ALGO_8,
+    TECOOPS_ALGO_9,
+} tecoopsAlgo_t;
+
+/* reference: tecoops.h:73-85 */
+typedef enum {
+    TECOOPS_DATA_FLOAT = 0,
+    TECOOPS_DATA_HALF = 1,
+    TECOOPS_DATA_INT8 = 2,
+    TECOOPS_DATA_INT16 = 3,
+    TECOOPS_DATA_INT32 = 4,
+    TECOOPS_DATA_INT64 = 5,
+    TECOOPS_DATA_UINT8 = 6,
+    TECOOPS_DATA_BOOL = 7,
+    TECOOPS_DATA_DOUBLE = 8,
+    TECOOPS_DATA_BFLOAT16 = 9,
+    TECOOPS_DATA_COMPLEX_FLOAT = 10,
+} tecoopsDataType_t;
+
+typedef struct tecoopsContext *tecoopsHandle_t;
+typedef struct tecoopsTensorStruct *tecoopsTensorDescriptor_t;
+
+/* ---- handle (reference: tecoops.h:90-94; interface/common/tecoops.cpp:38-76) ---- */
+tecoopsStatus_t tecoopsCreate(tecoopsHandle_t *handle);
+tecoopsStatus_t tecoopsDestroy(tecoopsHandle_t handle);
+tecoopsStatus_t tecoopsSetStream(tecoopsHandle_t handle, cudaStream_t stream);
+tecoopsStatus_t tecoopsGetStream(tecoopsHandle_t handle, cudaStream_t *stream);
+const char *tecoopsGetErrorString(tecoopsStatus_t status);
+
+/* ---- tensor descriptors (reference: tecoops.h:96-122; tecoops.cpp:78-237) ---- */
+tecoopsStatus_t tecoopsCreateTensorDescriptor(tecoopsTensorDescriptor_t *tensorDesc);
+tecoopsStatus_t tecoopsSetTensor4dDescriptor(tecoopsTensorDescriptor_t tensorDesc,
+                                             tecoopsTensorFormat_t format,
+                                             tecoopsDataType_t dataType,
+                                             int n, int c, int h, int w);
+tecoopsStatus_t tecoopsGetTensor4dDescriptor(const tecoopsTensorDescriptor_t tensorDesc,
+                                             tecoopsDataType_t *dataType,
+                                             int *n, int *c, int *h, int *w,
+                                             int *nStride, int *cStride, int *hStride,
+                                             int *wStride);
+tecoopsStatus_t tecoopsSetTensorNdDescriptor(tecoopsTensorDescriptor_t tensorDesc,
+                                             tecoopsDataType_t dataType, int nbDims,
+                                             const int dimA[], const int strideA[]);
+tecoopsStatus_t tecoopsGetTensorNdDescriptor(const tecoopsTensorDescriptor_t tensorDesc,
+                                             int nbDimsRequested, tecoopsDataType_t *dataType,
+                                             int *nbDims, int dimA[], int strideA[]);
+tecoopsStatus_t tecoopsDestroyTensorDescriptor(tecoopsTensorDescriptor_t tensorDesc);
+
+/* ---- memset (reference: tecoops.h:128; used by the reshape plugin) ---- */
+tecoopsStatus_t tecoopsMemset(tecoopsHandle_t handle, void *x, const int value, size_t size);
+
+/*
+ * reshape_and_cache — scatter K/V rows into the paged cache.
+ * Replaces reference tecoops.h:130-136 (teco/interface/ops/reshape_and_cache.cpp:64-105).
+ *   key, value    : [num_tokens, num_kv_heads, head_size], 2-byte elements (fp16 or bf16)
+ *   slot_mapping  : int64 [num_tokens]; slot < 0 means "padding, skip"
+ *   key_cache,
+ *   value_cache   : [num_blocks, num_kv_heads, block_size, head_size]
+ *   cache[slot / block_size][h][slot % block_size][:] = key[t][h][:]
+ * The copy is bit-exact.  Slots >= num_blocks*block_size are skipped too (the
+ * reference writes out of bounds there).  Two tokens mapped to the same slot
+ * race, as in the reference.
+ */
+tecoopsStatus_t tecoopsReshapeAndCache(tecoopsHandle_t handle,
+                                       const void *key, const void *value,
+                                       const int64_t *slot_mapping,
+                                       void *key_cache, void *value_cache,
+                                       int num_tokens, int num_kv_heads, int head_size,
+                                       int num_blocks, int block_size);
+
+/*
+ * flash_attention — paged, varlen, causal (bottom-right aligned), GQA attention
+ * with softmax scale 1/sqrt(head_size).
+ * Replaces reference tecoops.h:156-169 (teco/interface/ops/flash_attention.cpp:71-119).
+ *   q_seq_lens, kv_seq_lens : DEVICE int32 [batch] (lengths, not offsets); q_len <= kv_len
+ *   blockTableDesc/blockTable: int32 [batch, block_table_dim]
+ *   qDataDesc/qData, oDataDesc/oData : [sum(q_len), num_heads, head_size]
+ *   k/vCacheDesc, k/vCache : [num_blocks, num_kv_heads, block_size, head_size]
+ *   dtype: TECOOPS_DATA_HALF (reference) or TECOOPS_DATA_BFLOAT16 (extension)
+ *   max_seqlen_q == 1 selects the split-KV decode kernel; anything else the
+ *   tcgen05 prefill kernel (chunked and mixed batches included).
+ *   workspace: optional device scratch of at least
+ *   tecoopsGetFlashAttentionWorkspaceSize() bytes; nullptr makes the handle
+ *   allocate (and keep) its own scratch on first use.
+ */
+tecoopsStatus_t tecoopsFlashAttention(tecoopsHandle_t handle,
+                                      int max_seqlen_q, int max_seqlen_k,
+                                      int max_block_num, const int *q_seq_lens,
+                                      const int *kv_seq_lens,
+                                      const tecoopsTensorDescriptor_t blockTableDesc,
+                                      const void *blockTable,
+                                      const tecoopsTensorDescriptor_t qDataDesc,
+                                      const void *qData,
+                                      const tecoopsTensorDescriptor_t kCacheDesc,
+                                      const void *kCache,
+                                      const tecoopsTensorDescriptor_t vCacheDesc,
+                                      const void *vCache,
+                                      const tecoopsTensorDescriptor_t oDataDesc,
+                                      void *oData, void *workspace);
+
+/*
+ * Extension (no counterpart in the reference, whose `workspace` is always
+ * nullptr): bytes of device scratch tecoopsFlashAttention needs for these
+ * shapes, so that a caller can pass its own `workspace`.
+ */
+tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(tecoopsHandle_t handle,
+                                                      int max_seqlen_q, int max_seqlen_k,
+                                                      const tecoopsTensorDescriptor_t blockTableDesc,
+                                                      const tecoopsTensorDescriptor_t qDataDesc,
+                                                      const tecoopsTensorDescriptor_t kCacheDesc,
+                                                      size_t *workspace_bytes);
+
+/*
+ * Extension: status of the last device-side check of this handle's stream
+ * (bounded waits that gave up).  Synchronises the handle's stream.
+ * Returns TECOOPS_STATUS_INTERNAL_ERROR if a kernel reported an error since the
+ * previous call (and clears it), TECOOPS_STATUS_SUCCESS otherwise.
+ */
+tecoopsStatus_t tecoopsGetDeviceErrorStatus(tecoopsHandle_t handle, int *error_code);
+
+/* ---- reference operators off this path: exported, NOT_SUPPORTED ---- */
+tecoopsStatus_t tecoopsFlattenRays(tecoopsHandle_t handle, const int *rays, uint32_t N,
+                                   uint32_t M, int *res, tecoopsAlgo_t algo);
+tecoopsStatus_t tecoopsReduceVariance(const tecoopsHandle_t handle, int axis, int correction,
+                                      const tecoopsTensorDescriptor_t xDesc, const void *x,
+                                      const tecoopsTensorDescriptor_t yDesc, void *y);
+tecoopsStatus_t tecoopsMorton3DInvert(tecoopsHandle_t handle, const int *indices, uint32_t N,
+                                      int *coords);
+tecoopsStatus_t tecoopsRmsNorm(tecoopsHandle_t handle, const void *input, const void *weight,
+                               const void *residual, void *output, void *residual_out,
+                               int num_tokens, int hidden_size, float eps);
+tecoopsStatus_t tecoopsCausalConv1d(tecoopsHandle_t handle, int batch, int totalSeqLen,
+                                    int dim, int width, int convStateStride, int xSeqStride,
+                                    int outSeqStride, int padSlotId, int api_mode, int actMode,
+                                    const void *x, void *convState, const void *weight,
+                                    void *out, const int *queryStartLoc,
+                                    const int *convStateIndices,
+                                    const int8_t *hasInitialState);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TECOOPS_B200_INCLUDE_TECOOPS_H_ */

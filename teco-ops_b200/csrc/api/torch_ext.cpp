@@ -1,0 +1,192 @@
+// PyTorch binding of the tecoops C API (module `tecoops._torch_ext`).
+//
+// Drop-in for reference api/torch_ext.cpp:
+//   * pybind names kept: reshape_and_cache (61-79) and flash_attn_varlen_func
+//     (99-165, same 14 positional arguments) — torch_ext.cpp:208-215;
+//   * added, as the survey's north star asks: TORCH_LIBRARY(tecoops) ops
+//     torch.ops.tecoops.reshape_and_cache / torch.ops.tecoops.flash_attention.
+// Differences from the reference binding (all B200-motivated):
+//   * q_seq_lens = diff(cu_seqlens_q) is computed ON THE DEVICE (the reference
+//     copies cu_seqlens_q to the host and back, a sync per call, 118-126);
+//   * one handle per (host thread, device); its stream is set to PyTorch's
+//     current CUDA stream on every call (the reference uses one global handle on
+//     the default stream, 35-42);
+//   * dtypes fp16 and bf16 (the reference hard-codes HALF descriptors);
+//   * `out` is not zero-filled first: every row inside a sequence is written,
+//     rows past sum(q_lens) are left untouched; an undefined/empty `out` is
+//     allocated (zeros) and returned;
+//   * softmax_scale / causal / window_size / return_softmax_lse are accepted and
+//     ignored exactly like the reference (scale is always 1/sqrt(D), causal
+//     bottom-right masking always applies).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+#include <torch/library.h>
+
+#include <array>
+#include <vector>
+
+#include "tecoops.h"
+
+namespace {
+
+tecoopsHandle_t handleFor(int device) {
+    thread_local std::array<tecoopsHandle_t, 64> handles{};
+    TORCH_CHECK(device >= 0 && device < 64, "tecoops: device index out of range");
+    if (handles[device] == nullptr) {
+        c10::cuda::CUDAGuard g(device);
+        tecoopsStatus_t st = tecoopsCreate(&handles[device]);
+        TORCH_CHECK(st == TECOOPS_STATUS_SUCCESS, "tecoopsCreate failed: ",
+                    tecoopsGetErrorString(st));
+    }
+    tecoopsHandle_t h = handles[device];
+    tecoopsSetStream(h, at::cuda::getCurrentCUDAStream(device).stream());
+    return h;
+}
+
+tecoopsDataType_t dtypeOf(const torch::Tensor &t) {
+    switch (t.scalar_type()) {
+        case at::kHalf: return TECOOPS_DATA_HALF;
+        case at::kBFloat16: return TECOOPS_DATA_BFLOAT16;
+        case at::kInt: return TECOOPS_DATA_INT32;
+        case at::kLong: return TECOOPS_DATA_INT64;
+        case at::kFloat: return TECOOPS_DATA_FLOAT;
+        default: TORCH_CHECK(false, "tecoops: unsupported dtype ", t.scalar_type());
+    }
+    return TECOOPS_DATA_FLOAT;
+}
+
+void checkStatus(tecoopsStatus_t st, const char *what) {
+    TORCH_CHECK(st == TECOOPS_STATUS_SUCCESS, what, " failed: ", tecoopsGetErrorString(st));
+}
+
+struct Desc {
+    tecoopsTensorDescriptor_t d = nullptr;
+    explicit Desc(const torch::Tensor &t) {
+        tecoopsCreateTensorDescriptor(&d);
+        std::vector<int> dims(t.dim());
+        for (int i = 0; i < t.dim(); ++i) dims[i] = static_cast<int>(t.size(i));
+        checkStatus(tecoopsSetTensorNdDescriptor(d, dtypeOf(t), t.dim(), dims.data(), nullptr),
+                    "tecoopsSetTensorNdDescriptor");
+    }
+    ~Desc() { tecoopsDestroyTensorDescriptor(d); }
+};
+
+void checkCuda(const torch::Tensor &t, const char *name) {
+    TORCH_CHECK(t.is_cuda(), "tecoops: ", name, " must be a CUDA tensor");
+    TORCH_CHECK(t.is_contiguous(), "tecoops: ", name, " must be contiguous");
+}
+
+}  // namespace
+
+void reshape_and_cache_torch(torch::Tensor key, torch::Tensor value, torch::Tensor slot_mapping,
+                             torch::Tensor key_cache, torch::Tensor value_cache) {
+    checkCuda(key, "key");
+    checkCuda(value, "value");
+    checkCuda(slot_mapping, "slot_mapping");
+    checkCuda(key_cache, "key_cache");
+    checkCuda(value_cache, "value_cache");
+    TORCH_CHECK(key.dim() == 3 && value.sizes() == key.sizes(), "key/value must be [T, H, D]");
+    TORCH_CHECK(key_cache.dim() == 4 && value_cache.sizes() == key_cache.sizes(),
+                "caches must be [num_blocks, num_kv_heads, block_size, head_size]");
+    TORCH_CHECK(key.element_size() == 2 && key_cache.scalar_type() == key.scalar_type() &&
+                    value.scalar_type() == key.scalar_type() &&
+                    value_cache.scalar_type() == key.scalar_type(),
+                "key/value/caches must share one 2-byte dtype");
+    TORCH_CHECK(slot_mapping.scalar_type() == at::kLong, "slot_mapping must be int64");
+    TORCH_CHECK(key_cache.size(1) == key.size(1) && key_cache.size(3) == key.size(2),
+                "cache head/dim mismatch");
+    TORCH_CHECK(slot_mapping.numel() >= key.size(0), "slot_mapping shorter than num_tokens");
+    if (key.size(0) == 0) return;
+    c10::cuda::CUDAGuard g(key.device());
+    tecoopsHandle_t h = handleFor(key.get_device());
+    checkStatus(tecoopsReshapeAndCache(h, key.data_ptr(), value.data_ptr(),
+                                       slot_mapping.data_ptr<int64_t>(), key_cache.data_ptr(),
+                                       value_cache.data_ptr(), (int)key.size(0), (int)key.size(1),
+                                       (int)key.size(2), (int)key_cache.size(0),
+                                       (int)key_cache.size(2)),
+                "tecoopsReshapeAndCache");
+}
+
+static torch::Tensor run_flash(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                               torch::Tensor q_lens, torch::Tensor kv_lens,
+                               torch::Tensor block_table, int64_t max_seqlen_q,
+                               int64_t max_seqlen_k, torch::Tensor out) {
+    checkCuda(q, "q");
+    checkCuda(k, "k_cache");
+    checkCuda(v, "v_cache");
+    checkCuda(block_table, "block_table");
+    TORCH_CHECK(block_table.scalar_type() == at::kInt, "block_table must be int32");
+    TORCH_CHECK(kv_lens.scalar_type() == at::kInt && q_lens.scalar_type() == at::kInt,
+                "sequence lengths must be int32");
+    if (!out.defined() || out.numel() == 0) out = torch::zeros_like(q);
+    checkCuda(out, "out");
+    c10::cuda::CUDAGuard g(q.device());
+    tecoopsHandle_t h = handleFor(q.get_device());
+    Desc bt(block_table), qd(q), kd(k), vd(v), od(out);
+    checkStatus(tecoopsFlashAttention(h, (int)max_seqlen_q, (int)max_seqlen_k, (int)k.size(0),
+                                      q_lens.data_ptr<int>(), kv_lens.data_ptr<int>(), bt.d,
+                                      block_table.data_ptr(), qd.d, q.data_ptr(), kd.d,
+                                      k.data_ptr(), vd.d, v.data_ptr(), od.d, out.data_ptr(),
+                                      nullptr),
+                "tecoopsFlashAttention");
+    return out;
+}
+
+torch::Tensor flash_attn_varlen_func_torch(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                           int64_t max_seqlen_q, torch::Tensor cu_seqlens_q,
+                                           int64_t max_seqlen_k, torch::Tensor cu_seqlens_k,
+                                           torch::Tensor seqused_k, double softmax_scale,
+                                           bool causal, torch::Tensor window_size,
+                                           torch::Tensor block_table, bool return_softmax_lse,
+                                           torch::Tensor out) {
+    (void)cu_seqlens_k;
+    (void)softmax_scale;
+    (void)causal;
+    (void)window_size;
+    (void)return_softmax_lse;
+    const int64_t batch = seqused_k.size(0);
+    TORCH_CHECK(cu_seqlens_q.numel() >= batch + 1, "cu_seqlens_q must hold batch + 1 offsets");
+    auto cu = cu_seqlens_q.to(at::kInt);
+    // per-sequence query lengths, computed on the device (no host round trip)
+    auto q_lens = (cu.slice(0, 1, batch + 1) - cu.slice(0, 0, batch)).contiguous();
+    auto kv_lens = seqused_k.to(at::kInt).contiguous();
+    return run_flash(q, k, v, q_lens, kv_lens, block_table, max_seqlen_q, max_seqlen_k, out);
+}
+
+// torch.ops.tecoops.* (C-API argument meaning: lengths, not offsets)
+void reshape_and_cache_op(const at::Tensor &key, const at::Tensor &value,
+                          const at::Tensor &slot_mapping, at::Tensor key_cache,
+                          at::Tensor value_cache) {
+    reshape_and_cache_torch(key, value, slot_mapping, key_cache, value_cache);
+}
+
+void flash_attention_op(const at::Tensor &q, const at::Tensor &k_cache,
+                        const at::Tensor &v_cache, const at::Tensor &q_seq_lens,
+                        const at::Tensor &kv_seq_lens, const at::Tensor &block_table,
+                        int64_t max_seqlen_q, int64_t max_seqlen_k, at::Tensor out) {
+    TORCH_CHECK(out.defined() && out.sizes() == q.sizes(), "out must have the shape of q");
+    run_flash(q, k_cache, v_cache, q_seq_lens.contiguous(), kv_seq_lens.contiguous(),
+              block_table, max_seqlen_q, max_seqlen_k, out);
+}
+
+TORCH_LIBRARY(tecoops, m) {
+    m.def(
+        "reshape_and_cache(Tensor key, Tensor value, Tensor slot_mapping, Tensor(a!) key_cache, "
+        "Tensor(b!) value_cache) -> ()");
+    m.def(
+        "flash_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor q_seq_lens, "
+        "Tensor kv_seq_lens, Tensor block_table, int max_seqlen_q, int max_seqlen_k, "
+        "Tensor(a!) out) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(tecoops, CUDA, m) {
+    m.impl("reshape_and_cache", &reshape_and_cache_op);
+    m.impl("flash_attention", &flash_attention_op);
+}
+
+PYBIND11_MODULE(_torch_ext, m) {
+    m.def("reshape_and_cache", &reshape_and_cache_torch, "reshape_and_cache (sm_100a)");
+    m.def("flash_attn_varlen_func", &flash_attn_varlen_func_torch,
+          "flash_attn_varlen_func (sm_100a)");
+}

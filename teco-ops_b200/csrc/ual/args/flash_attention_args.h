@@ -1,0 +1,53 @@
+// Argument blocks of the flash-attention kernel launchers.
+// Mirrors reference teco/ual/args/flash_attention_args.h:37-62
+// (FlashAttentionArgs / FlashAttentionPatchArgs).  `spe_num` becomes the SM
+// count, `workspace` is actually used (split-KV partials and the prefill tile
+// scheduler), and the dtype is carried so that fp16 and bf16 both dispatch.
+#ifndef TECOOPS_B200_UAL_ARGS_FLASH_ATTENTION_ARGS_H_
+#define TECOOPS_B200_UAL_ARGS_FLASH_ATTENTION_ARGS_H_
+
+#include <cstddef>
+#include <cstdint>
+
+namespace tecoops {
+namespace ual {
+namespace args {
+
+enum class ElemType { F16 = 0, BF16 = 1 };
+
+struct FlashAttentionArgs {
+    int num_sms;
+    int batch_size;
+    int size_per_head;       // D
+    int local_head_num;      // Hq
+    int local_kv_head_num;   // Hkv
+    int block_size;          // tokens per cache page
+    int block_table_dim;     // pages per block_table row
+    int max_q_seq_len;
+    int max_k_seq_len;
+    int max_block_num;       // pages in the cache pool
+    int total_q;             // rows of q / out
+    float softmax_scale;
+    ElemType dtype;
+    const int *q_seq_lens;   // device [batch]
+    const int *kv_seq_lens;  // device [batch]
+    const int *block_table;  // device [batch, block_table_dim]
+    const void *q;           // [total_q, Hq, D]
+    const void *key_cache;   // [max_block_num, Hkv, block_size, D]
+    const void *value_cache;
+    void *fmha_out;          // [total_q, Hq, D]
+    void *workspace;         // device scratch (size from the op's workspaceSize)
+    size_t workspace_bytes;
+    int *dev_error;          // error word for bounded waits (may be null)
+};
+
+// Branch selection input (reference FlashAttentionPatchArgs).
+struct FlashAttentionPatchArgs {
+    const FlashAttentionArgs *rvargs;
+};
+
+}  // namespace args
+}  // namespace ual
+}  // namespace tecoops
+
+#endif  // TECOOPS_B200_UAL_ARGS_FLASH_ATTENTION_ARGS_H_

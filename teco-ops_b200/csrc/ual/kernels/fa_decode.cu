@@ -1,0 +1,373 @@
+// Paged single-token decode attention for sm_100a (split-KV / flash-decoding).
+//
+// Semantics: the reference kernel teco/ual/kernel/flash_attention/flash_attention.scpp
+// (179-416) with q_len == 1, as pinned by its golden
+// test/zoo/teco/flash_attention/flash_attention.py:79-140: one query row per sequence
+// attends to all kv_len cached tokens (bottom-right causal with L == 1), keys and
+// values gathered page by page through block_table, scale 1/sqrt(D), GQA head
+// h -> kv head h / (Hq/Hkv).
+//
+// B200 design (bandwidth-bound: ~4 FLOP per cache byte):
+//  * one CTA per (sequence, KV head, 16-head Q slice, KV split).  All Q heads of
+//    a GQA group are packed into the 16 rows of one warp MMA tile so every K/V
+//    byte is read from HBM exactly once;
+//  * the KV range of a sequence is cut into splits of `split_tokens` so that even
+//    64 sequences fill 148 SMs; each CTA streams its pages through a 3-stage
+//    cp.async ring (64 tokens x K and V per stage, XOR-swizzled 16-byte chunks so
+//    ldmatrix is bank-conflict free), 4 warps each own 16 tokens of a stage;
+//  * QK^T and PV on the warp MMA (m16n8k16, fp32 accumulate), online softmax in
+//    registers in the exp2 domain, P kept in registers as the A operand;
+//  * the 4 warps merge through shared memory; a sequence that needs one split
+//    writes its output directly, otherwise (O/l, log2-sum-exp) partials go to
+//    the workspace and fa_decode_merge combines them.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "ual/kernels/common.cuh"
+#include "ual/kernels/launchers.h"
+
+namespace tecoops {
+namespace kern {
+
+namespace {
+
+constexpr int kStageTokens = 64;   // tokens per pipeline stage (4 warps x 16)
+constexpr int kStages = 3;
+constexpr int kThreads = 128;
+
+template <int D>
+struct DecodeSmem {
+    static constexpr int kRowBytes = D * 2;
+    static constexpr int kTileBytes = kStageTokens * kRowBytes;   // one of K or V
+    static constexpr int kStageBytes = 2 * kTileBytes;
+    static constexpr int kPipeBytes = kStages * kStageBytes;
+    static constexpr int kMergeBytes = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
+    static constexpr int kBytes = kPipeBytes > kMergeBytes ? kPipeBytes : kMergeBytes;
+};
+
+// byte offset of 16-byte chunk `ch` of row `r` inside a [64][D] tile
+template <int D>
+__device__ __forceinline__ uint32_t swz(int r, int ch) {
+    return (uint32_t)(r * (D * 2) + ((ch ^ (r & 7)) << 4));
+}
+
+}  // namespace
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 2) fa_decode_splitkv_kernel(DecodeParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    using Sm = DecodeSmem<D>;
+    constexpr int kChunks = D / 8;   // 16-byte chunks per row
+
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.num_slices;
+    const int slice = blockIdx.y - kvh * p.num_slices;
+    const int b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+
+    const int q_len = __ldg(p.q_seq_lens + b);
+    const int kv_len = __ldg(p.kv_seq_lens + b);
+    if (q_len <= 0) return;
+    const int kv_begin = split * p.split_tokens;
+    const int n_split_b = (kv_len + p.split_tokens - 1) / p.split_tokens;
+    if (kv_begin >= kv_len && !(split == 0 && kv_len <= 0)) return;
+    const int kv_end = min(kv_len, kv_begin + p.split_tokens);
+    const int qrow = warp_seq_start(p.q_seq_lens, b);   // q_len == 1 on this path
+
+    const int head0 = kvh * p.group + slice * 16;              // first q head of this tile
+    const int rows = min(16, p.group - slice * 16);            // valid q heads
+
+    // ---- Q fragments (A operand), rows >= `rows` are zero ---------------------
+    const int g = lane >> 2;
+    const int c = lane & 3;
+    uint32_t qa[D / 16][4];
+    {
+        const T *qbase = static_cast<const T *>(p.q) + ((int64_t)qrow * p.num_heads + head0) * D;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+            const int k0 = kk * 16 + 2 * c;
+            const uint32_t *r0 = reinterpret_cast<const uint32_t *>(qbase + (int64_t)g * D + k0);
+            const uint32_t *r1 =
+                reinterpret_cast<const uint32_t *>(qbase + (int64_t)(g + 8) * D + k0);
+            qa[kk][0] = g < rows ? __ldg(r0) : 0u;
+            qa[kk][1] = g + 8 < rows ? __ldg(r1) : 0u;
+            qa[kk][2] = g < rows ? __ldg(r0 + 4) : 0u;
+            qa[kk][3] = g + 8 < rows ? __ldg(r1 + 4) : 0u;
+        }
+    }
+
+    const T *kc = static_cast<const T *>(p.key_cache);
+    const T *vc = static_cast<const T *>(p.value_cache);
+    const int *bt = p.block_table + (int64_t)b * p.block_table_dim;
+    const int64_t page_stride = (int64_t)p.num_kv_heads * p.block_size * D;   // elements
+    const int64_t head_off = (int64_t)kvh * p.block_size * D;
+
+    const int n_iters = (kv_end - kv_begin + kStageTokens - 1) / kStageTokens;
+    const uint32_t smem_base = smem_u32(smem);
+
+    auto issue_stage = [&](int it) {
+        const int buf = it % kStages;
+        const uint32_t kdst = smem_base + buf * Sm::kStageBytes;
+        const uint32_t vdst = kdst + Sm::kTileBytes;
+        const int t0 = kv_begin + it * kStageTokens;
+#pragma unroll
+        for (int i = 0; i < (kStageTokens * kChunks) / kThreads; ++i) {
+            const int id = tid + i * kThreads;
+            const int r = id / kChunks;
+            const int ch = id - r * kChunks;
+            const int tok = t0 + r;
+            const bool valid = tok < kv_end;
+            int64_t off = 0;
+            if (valid) {
+                const int blk = __ldg(bt + tok / p.block_size);
+                const int in_page = tok - (tok / p.block_size) * p.block_size;
+                off = (int64_t)blk * page_stride + head_off + (int64_t)in_page * D + ch * 8;
+            }
+            const int nbytes = valid ? 16 : 0;
+            cp_async16(kdst + swz<D>(r, ch), kc + off, nbytes);
+            cp_async16(vdst + swz<D>(r, ch), vc + off, nbytes);
+        }
+    };
+
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (s < n_iters) issue_stage(s);
+        cp_async_commit();
+    }
+
+    float m_r[2] = {-INFINITY, -INFINITY};
+    float l_r[2] = {0.f, 0.f};
+    float o[D / 8][4];
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+    const float sl2 = p.scale_log2;
+    const int mi = lane >> 3;   // ldmatrix matrix index of this lane's address
+    const int ri = lane & 7;
+
+    for (int it = 0; it < n_iters; ++it) {
+        if (it + kStages - 1 < n_iters) issue_stage(it + kStages - 1);
+        cp_async_commit();
+        cp_async_wait<kStages - 1>();
+        __syncthreads();
+
+        const int buf = it % kStages;
+        const uint32_t ktile = smem_base + buf * Sm::kStageBytes;
+        const uint32_t vtile = ktile + Sm::kTileBytes;
+        const int wrow = warp * 16;
+        const int tok_base = kv_begin + it * kStageTokens + wrow;
+
+        if (tok_base < kv_end) {
+            // S = Q K^T for this warp's 16 tokens: two n-tiles of 8 tokens
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t kb[4];
+                const int r = wrow + (mi >> 1) * 8 + ri;
+                ldmatrix_x4(kb, ktile + swz<D>(r, 2 * kk + (mi & 1)));
+                mma16816<T>(s[0], qa[kk], kb[0], kb[1]);
+                mma16816<T>(s[1], qa[kk], kb[2], kb[3]);
+            }
+            // scale, mask the ragged tail, online softmax (rows g and g+8)
+            float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int tok = tok_base + 8 * j + 2 * c + (e & 1);
+                    const float x = tok < kv_end ? s[j][e] * sl2 : -INFINITY;
+                    s[j][e] = x;
+                    mx[e >> 1] = fmaxf(mx[e >> 1], x);
+                }
+            }
+            float alpha[2], mu[2];
+#pragma unroll
+            for (int r2 = 0; r2 < 2; ++r2) {
+                mx[r2] = fmaxf(mx[r2], __shfl_xor_sync(0xffffffffu, mx[r2], 1));
+                mx[r2] = fmaxf(mx[r2], __shfl_xor_sync(0xffffffffu, mx[r2], 2));
+                const float m_new = fmaxf(m_r[r2], mx[r2]);
+                mu[r2] = m_new == -INFINITY ? 0.f : m_new;
+                alpha[r2] = fast_exp2(m_r[r2] - mu[r2]);
+                m_r[r2] = m_new;
+            }
+            float ps[2] = {0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float pe = fast_exp2(s[j][e] - mu[e >> 1]);
+                    s[j][e] = pe;
+                    ps[e >> 1] += pe;
+                }
+            }
+            l_r[0] = l_r[0] * alpha[0] + ps[0];
+            l_r[1] = l_r[1] * alpha[1] + ps[1];
+#pragma unroll
+            for (int n = 0; n < D / 8; ++n) {
+                o[n][0] *= alpha[0];
+                o[n][1] *= alpha[0];
+                o[n][2] *= alpha[1];
+                o[n][3] *= alpha[1];
+            }
+            uint32_t pa[4];
+            pa[0] = Elem<T>::pack2(s[0][0], s[0][1]);
+            pa[1] = Elem<T>::pack2(s[0][2], s[0][3]);
+            pa[2] = Elem<T>::pack2(s[1][0], s[1][1]);
+            pa[3] = Elem<T>::pack2(s[1][2], s[1][3]);
+            // O += P V
+#pragma unroll
+            for (int nn = 0; nn < D / 16; ++nn) {
+                uint32_t vb[4];
+                const int r = wrow + (mi & 1) * 8 + ri;
+                ldmatrix_x4_trans(vb, vtile + swz<D>(r, 2 * nn + (mi >> 1)));
+                mma16816<T>(o[2 * nn], pa, vb[0], vb[1]);
+                mma16816<T>(o[2 * nn + 1], pa, vb[2], vb[3]);
+            }
+        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+
+    // ---- merge the 4 warps through shared memory ------------------------------
+    l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
+    l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
+    l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
+    l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
+
+    float *so = reinterpret_cast<float *>(smem);               // [4][16][D]
+    float *sml = so + 4 * 16 * D;                               // [4][16][2]
+    __syncthreads();
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+        const int col = n * 8 + 2 * c;
+        so[(warp * 16 + g) * D + col] = o[n][0];
+        so[(warp * 16 + g) * D + col + 1] = o[n][1];
+        so[(warp * 16 + g + 8) * D + col] = o[n][2];
+        so[(warp * 16 + g + 8) * D + col + 1] = o[n][3];
+    }
+    if (c == 0) {
+        sml[(warp * 16 + g) * 2 + 0] = m_r[0];
+        sml[(warp * 16 + g) * 2 + 1] = l_r[0];
+        sml[(warp * 16 + g + 8) * 2 + 0] = m_r[1];
+        sml[(warp * 16 + g + 8) * 2 + 1] = l_r[1];
+    }
+    __syncthreads();
+
+    const bool direct = n_split_b <= 1;
+    for (int idx = tid; idx < rows * D; idx += kThreads) {
+        const int r = idx / D;
+        const int d = idx - r * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, sml[(w * 16 + r) * 2]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float f = fast_exp2(sml[(w * 16 + r) * 2] - Mu);
+            L += sml[(w * 16 + r) * 2 + 1] * f;
+            O += so[(w * 16 + r) * D + d] * f;
+        }
+        const float val = L > 0.f ? O / L : 0.f;
+        const int h = head0 + r;
+        if (direct) {
+            T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * D + d;
+            *out = Elem<T>::from_float(val);
+        } else {
+            const int64_t rec = ((int64_t)b * p.num_heads + h) * p.max_splits + split;
+            p.part_o[rec * D + d] = val;
+            if (d == 0) p.part_lse[rec] = L > 0.f ? Mu + log2f(L) : -INFINITY;
+        }
+    }
+}
+
+// Combine the split partials of every (sequence, q head) that used more than
+// one split: out = sum_s 2^(lse_s - M) O_s / sum_s 2^(lse_s - M).
+template <typename T>
+__global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
+    const int b = blockIdx.x / p.num_heads;
+    const int h = blockIdx.x - b * p.num_heads;
+    const int q_len = __ldg(p.q_seq_lens + b);
+    const int kv_len = __ldg(p.kv_seq_lens + b);
+    const int ns = (kv_len + p.split_tokens - 1) / p.split_tokens;
+    if (q_len <= 0 || ns <= 1) return;
+    const int qrow = warp_seq_start(p.q_seq_lens, b);
+    const int64_t rec0 = ((int64_t)b * p.num_heads + h) * p.max_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, p.part_lse[rec0 + s]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+    for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
+        float W = 0.f, O = 0.f;
+        for (int s = 0; s < ns; ++s) {
+            const float w = fast_exp2(p.part_lse[rec0 + s] - Mu);
+            W += w;
+            O += w * p.part_o[(rec0 + s) * p.head_dim + d];
+        }
+        T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * p.head_dim + d;
+        *out = Elem<T>::from_float(W > 0.f ? O / W : 0.f);
+    }
+}
+
+// ---- host side ------------------------------------------------------------------
+
+bool decode_supported(int head_dim, int block_size, int group) {
+    (void)group;
+    return (head_dim == 64 || head_dim == 128) && block_size > 0 && (block_size % 16 == 0);
+}
+
+void decode_plan(int num_sms, int batch, int kv_heads, int group, int max_k, int *split_tokens,
+                 int *max_splits) {
+    const int slices = (group + 15) / 16;
+    const int64_t work = (int64_t)batch * kv_heads * slices * (int64_t)(max_k > 0 ? max_k : 1);
+    const int64_t target = (int64_t)num_sms * 2 * 8;   // ~8 waves of 2 CTAs per SM
+    int64_t split = (work + target - 1) / target;
+    split = ((split + kStageTokens - 1) / kStageTokens) * kStageTokens;
+    if (split < 256) split = 256;
+    const int64_t cap = ((int64_t)(max_k > 0 ? max_k : 1) + kStageTokens - 1) / kStageTokens *
+                        kStageTokens;
+    if (split > cap) split = cap < kStageTokens ? kStageTokens : cap;
+    *split_tokens = (int)split;
+    *max_splits = (int)(((max_k > 0 ? max_k : 1) + split - 1) / split);
+}
+
+size_t decode_workspace_bytes(int batch, int num_heads, int head_dim, int max_splits) {
+    if (max_splits <= 1) return 0;
+    const size_t recs = (size_t)batch * num_heads * max_splits;
+    return recs * head_dim * sizeof(float) + recs * sizeof(float) + 256;
+}
+
+template <typename T, int D>
+static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
+    const int smem = DecodeSmem<D>::kBytes;
+    auto kfn = fa_decode_splitkv_kernel<T, D>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.max_splits, p.num_kv_heads * p.num_slices, p.batch);
+    kfn<<<grid, kThreads, smem, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (p.max_splits > 1) {
+        fa_decode_merge_kernel<T><<<p.batch * p.num_heads, 128, 0, stream>>>(p);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+cudaError_t launch_decode(const DecodeParams &p, bool bf16, cudaStream_t stream) {
+    if (p.head_dim == 128) {
+        return bf16 ? launch_decode_t<__nv_bfloat16, 128>(p, stream)
+                    : launch_decode_t<__half, 128>(p, stream);
+    }
+    if (p.head_dim == 64) {
+        return bf16 ? launch_decode_t<__nv_bfloat16, 64>(p, stream)
+                    : launch_decode_t<__half, 64>(p, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace kern
+}  // namespace tecoops

@@ -1,0 +1,125 @@
+// Shape-generic paged attention (any head_dim <= 256, any block_size, any GQA
+// ratio).  It serves shapes the tuned kernels do not cover (block_size not a
+// multiple of 16, head_dim outside {64, 128}); it is a GPU kernel, not a
+// host fallback.
+//
+// Semantics: reference golden test/zoo/teco/flash_attention/flash_attention.py:79-140
+// (bottom-right causal: row i of a sequence with q_len L and kv_len S attends keys
+// j <= S - L + i; scale 1/sqrt(D); q head h reads kv head h / (Hq/Hkv)).
+//
+// One warp per (query row, q head).  Keys are taken 32 at a time, one key per
+// lane for the dot product, then the lanes switch to owning head dimensions for
+// the P.V accumulation; online softmax in the exp2 domain.
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "ual/kernels/common.cuh"
+#include "ual/kernels/launchers.h"
+
+namespace tecoops {
+namespace kern {
+
+template <typename T>
+__global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
+    constexpr int kMaxD = 256;
+    __shared__ float qs[4][kMaxD];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t pair = (int64_t)blockIdx.x * 4 + warp;
+    if (pair >= (int64_t)s.total_q * s.num_heads) return;
+    const int row = (int)(pair / s.num_heads);
+    const int h = (int)(pair - (int64_t)row * s.num_heads);
+    const int D = s.head_dim;
+
+    // locate the sequence of this row
+    int b = 0, start = 0;
+    for (; b < s.batch; ++b) {
+        const int L = __ldg(s.q_seq_lens + b);
+        if (row < start + L) break;
+        start += L;
+    }
+    T *out = static_cast<T *>(s.out) + ((int64_t)row * s.num_heads + h) * D;
+    if (b >= s.batch) {   // row beyond sum(q_seq_lens): leave zeros
+        for (int d = lane; d < D; d += 32) out[d] = Elem<T>::from_float(0.f);
+        return;
+    }
+    const int L = __ldg(s.q_seq_lens + b);
+    const int S = __ldg(s.kv_seq_lens + b);
+    const int i = row - start;
+    int allowed = S - L + i + 1;
+    if (allowed > S) allowed = S;
+    const int kvh = h / (s.num_heads / s.num_kv_heads);
+
+    const T *q = static_cast<const T *>(s.q) + ((int64_t)row * s.num_heads + h) * D;
+    for (int d = lane; d < D; d += 32) qs[warp][d] = Elem<T>::to_float(q[d]);
+    __syncwarp();
+
+    const T *kc = static_cast<const T *>(s.key_cache);
+    const T *vc = static_cast<const T *>(s.value_cache);
+    const int *bt = s.block_table + (int64_t)b * s.block_table_dim;
+    const int64_t page_stride = (int64_t)s.num_kv_heads * s.block_size * D;
+    const int64_t head_off = (int64_t)kvh * s.block_size * D;
+
+    float m = -INFINITY, l = 0.f;
+    float acc[kMaxD / 32];
+#pragma unroll
+    for (int k = 0; k < kMaxD / 32; ++k) acc[k] = 0.f;
+
+    for (int j0 = 0; j0 < allowed; j0 += 32) {
+        const int j = j0 + lane;
+        float x = -INFINITY;
+        int64_t my_off = 0;
+        if (j < allowed) {
+            const int blk = __ldg(bt + j / s.block_size);
+            my_off = (int64_t)blk * page_stride + head_off + (int64_t)(j % s.block_size) * D;
+            float dot = 0.f;
+            for (int d = 0; d < D; ++d) dot += qs[warp][d] * Elem<T>::to_float(kc[my_off + d]);
+            x = dot * s.scale_log2;
+        }
+        float cm = x;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+        const float m_new = fmaxf(m, cm);
+        const float alpha = exp2f(m - m_new);
+        const float pj = (j < allowed) ? exp2f(x - m_new) : 0.f;
+        float ps = pj;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        l = l * alpha + ps;
+        m = m_new;
+#pragma unroll
+        for (int k = 0; k < kMaxD / 32; ++k) acc[k] *= alpha;
+        const int nvalid = min(32, allowed - j0);
+        for (int t = 0; t < nvalid; ++t) {
+            const float pt = __shfl_sync(0xffffffffu, pj, t);
+            const int64_t off = __shfl_sync(0xffffffffu, my_off, t);
+#pragma unroll
+            for (int k = 0; k < kMaxD / 32; ++k) {
+                const int d = lane + 32 * k;
+                if (d < D) acc[k] += pt * Elem<T>::to_float(vc[off + d]);
+            }
+        }
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxD / 32; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) out[d] = Elem<T>::from_float(acc[k] * inv);
+    }
+}
+
+cudaError_t launch_generic_attention(const AttnShape &s, bool bf16, cudaStream_t stream) {
+    if (s.head_dim > 256 || s.head_dim <= 0) return cudaErrorInvalidValue;
+    const int64_t pairs = (int64_t)s.total_q * s.num_heads;
+    if (pairs == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)((pairs + 3) / 4);
+    if (bf16)
+        fa_generic_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(s);
+    else
+        fa_generic_kernel<__half><<<grid, 128, 0, stream>>>(s);
+    return cudaGetLastError();
+}
+
+}  // namespace kern
+}  // namespace tecoops

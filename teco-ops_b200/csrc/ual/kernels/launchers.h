@@ -1,0 +1,85 @@
+// Host-side launch entry points of the device kernels (the UAL kernel table
+// points at these).  Parameter blocks are plain structs passed by value to the
+// kernels.
+#ifndef TECOOPS_B200_UAL_KERNELS_LAUNCHERS_H_
+#define TECOOPS_B200_UAL_KERNELS_LAUNCHERS_H_
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "ual/args/reshape_and_cache_args.h"
+
+namespace tecoops {
+namespace kern {
+
+// ---- reshape_and_cache ---------------------------------------------------------
+cudaError_t launch_reshape_and_cache(const ual::args::ReshapeAndCacheArgs &a, int num_sms,
+                                     cudaStream_t stream);
+
+// ---- paged attention: shared shape block ---------------------------------------
+struct AttnShape {
+    const void *q;            // [total_q, Hq, D]
+    const void *key_cache;    // [num_pages, Hkv, block_size, D]
+    const void *value_cache;
+    void *out;                // [total_q, Hq, D]
+    const int *q_seq_lens;    // [batch]
+    const int *kv_seq_lens;   // [batch]
+    const int *block_table;   // [batch, block_table_dim]
+    int batch;
+    int num_heads;
+    int num_kv_heads;
+    int head_dim;
+    int block_size;
+    int block_table_dim;
+    int num_pages;
+    int total_q;
+    int max_q;
+    int max_k;
+    float scale_log2;         // softmax_scale * log2(e)
+};
+
+// ---- split-KV decode -------------------------------------------------------------
+struct DecodeParams {
+    const void *q;
+    const void *key_cache;
+    const void *value_cache;
+    void *out;
+    const int *q_seq_lens;
+    const int *kv_seq_lens;
+    const int *block_table;
+    int batch;
+    int num_heads;
+    int num_kv_heads;
+    int group;          // num_heads / num_kv_heads
+    int num_slices;     // ceil(group / 16)
+    int head_dim;
+    int block_size;
+    int block_table_dim;
+    int split_tokens;   // multiple of 64
+    int max_splits;
+    float scale_log2;
+    float *part_o;      // [batch, Hq, max_splits, D]
+    float *part_lse;    // [batch, Hq, max_splits]
+};
+
+bool decode_supported(int head_dim, int block_size, int group);
+void decode_plan(int num_sms, int batch, int kv_heads, int group, int max_k, int *split_tokens,
+                 int *max_splits);
+size_t decode_workspace_bytes(int batch, int num_heads, int head_dim, int max_splits);
+cudaError_t launch_decode(const DecodeParams &p, bool bf16, cudaStream_t stream);
+
+// ---- tcgen05 prefill -------------------------------------------------------------
+bool prefill_supported(int head_dim, int block_size, int group);
+size_t prefill_workspace_bytes(const AttnShape &s);
+cudaError_t launch_prefill(const AttnShape &s, bool bf16, void *workspace, int *dev_error,
+                           int num_sms, cudaStream_t stream);
+
+// ---- generic (any head_dim <= 256, any block_size) --------------------------------
+cudaError_t launch_generic_attention(const AttnShape &s, bool bf16, cudaStream_t stream);
+
+}  // namespace kern
+}  // namespace tecoops
+
+#endif  // TECOOPS_B200_UAL_KERNELS_LAUNCHERS_H_

@@ -1,0 +1,161 @@
+// reshape_and_cache for sm_100a: scatter key/value rows into the paged cache.
+//
+// Semantics follow the reference kernel
+// teco/ual/kernel/reshape_and_cache/reshape_and_cache_fp16.scpp:47-96 and its CPU
+// golden test/zoo/teco/reshape_and_cache/reshape_and_cache.cpp:136-147:
+//   for token t, slot = slot_mapping[t]; slot < 0 -> skip;
+//   blk = slot / block_size, off = slot % block_size;
+//   for head h: key_cache[blk][h][off][:] = key[t][h][:]   (same for value)
+// The copy is a bit-exact move of 2-byte words.
+//
+// B200 design: the reference issues 2*H blocking 256-byte DMA copies per token
+// on 32 cores.  Here the whole [T, H, D] row space is flattened into 16-byte
+// vectors; each thread moves UNROLL vectors of K and of V per iteration with all
+// loads issued before any store (memory-level parallelism), loads bypass L1
+// (read-once data), consecutive lanes touch consecutive 16-byte pieces of the
+// same 256-byte head row, so both the reads and the scattered writes are whole
+// 32-byte sectors.  The grid is a multiple of the SM count.  64-bit offsets
+// throughout (caches beyond 2^31 elements).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "ual/args/reshape_and_cache_args.h"
+
+namespace tecoops {
+namespace kern {
+
+using ual::args::ReshapeAndCacheArgs;
+
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st16(void *p, const uint4 &v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Vectorised path: head_size*2 bytes is a multiple of 16 and every base pointer
+// and token stride is 16-byte aligned.
+template <int UNROLL>
+__global__ void __launch_bounds__(256) reshape_and_cache_vec16_kernel(
+    const uint8_t *__restrict__ key, const uint8_t *__restrict__ value,
+    const int64_t *__restrict__ slot_mapping, uint8_t *__restrict__ key_cache,
+    uint8_t *__restrict__ value_cache, int64_t total_vecs, int vecs_per_head, int heads,
+    int block_size, int64_t num_slots, int64_t key_stride_b, int64_t value_stride_b,
+    int64_t block_stride_b, int64_t head_stride_b, int64_t entry_stride_b) {
+    const int64_t vecs_per_token = (int64_t)vecs_per_head * heads;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+
+    for (; i0 < total_vecs; i0 += step * UNROLL) {
+        uint4 kv[UNROLL], vv[UNROLL];
+        int64_t dst[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int64_t i = i0 + (int64_t)u * step;
+            dst[u] = -1;
+            if (i < total_vecs) {
+                const int64_t t = i / vecs_per_token;
+                const int r = (int)(i - t * vecs_per_token);
+                const int h = r / vecs_per_head;
+                const int c = r - h * vecs_per_head;
+                const int64_t slot = __ldg(slot_mapping + t);
+                if (slot >= 0 && slot < num_slots) {
+                    const int64_t blk = slot / block_size;
+                    const int64_t off = slot - blk * block_size;
+                    dst[u] = blk * block_stride_b + h * head_stride_b + off * entry_stride_b +
+                             (int64_t)c * 16;
+                    const int64_t srck = t * key_stride_b + (int64_t)r * 16;
+                    const int64_t srcv = t * value_stride_b + (int64_t)r * 16;
+                    kv[u] = ld_stream16(key + srck);
+                    vv[u] = ld_stream16(value + srcv);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            if (dst[u] >= 0) {
+                st16(key_cache + dst[u], kv[u]);
+                st16(value_cache + dst[u], vv[u]);
+            }
+        }
+    }
+}
+
+// Generic path: any head_size / alignment, 2-byte words.
+__global__ void __launch_bounds__(256) reshape_and_cache_u16_kernel(
+    const uint16_t *__restrict__ key, const uint16_t *__restrict__ value,
+    const int64_t *__restrict__ slot_mapping, uint16_t *__restrict__ key_cache,
+    uint16_t *__restrict__ value_cache, int64_t total, int head_size, int heads, int block_size,
+    int64_t num_slots, int64_t key_stride, int64_t value_stride, int64_t block_stride,
+    int64_t head_stride, int64_t entry_stride) {
+    const int64_t per_token = (int64_t)head_size * heads;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / per_token;
+        const int r = (int)(i - t * per_token);
+        const int h = r / head_size;
+        const int d = r - h * head_size;
+        const int64_t slot = __ldg(slot_mapping + t);
+        if (slot < 0 || slot >= num_slots) continue;
+        const int64_t blk = slot / block_size;
+        const int64_t off = slot - blk * block_size;
+        const int64_t o = blk * block_stride + h * head_stride + off * entry_stride + d;
+        key_cache[o] = key[t * key_stride + r];
+        value_cache[o] = value[t * value_stride + r];
+    }
+}
+
+static inline bool aligned16(const void *p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+cudaError_t launch_reshape_and_cache(const ReshapeAndCacheArgs &a, int num_sms,
+                                     cudaStream_t stream) {
+    if (a.num_tokens <= 0) return cudaSuccess;
+    const int eb = a.elem_bytes;
+    const int64_t num_slots = (int64_t)a.num_blocks * a.block_size;
+    const int row_bytes = a.size_per_head * eb;
+    const bool vec = (row_bytes % 16 == 0) && aligned16(a.key) && aligned16(a.value) &&
+                     aligned16(a.key_cache) && aligned16(a.value_cache) &&
+                     ((a.key_stride * eb) % 16 == 0) && ((a.value_stride * eb) % 16 == 0);
+    if (vec) {
+        constexpr int kUnroll = 4;
+        const int vecs_per_head = row_bytes / 16;
+        const int64_t total = (int64_t)a.num_tokens * a.num_kv_heads * vecs_per_head;
+        const int threads = 256;
+        int64_t want = (total + (int64_t)threads * kUnroll - 1) / ((int64_t)threads * kUnroll);
+        const int64_t cap = (int64_t)num_sms * 8;   // 8 resident CTAs of 256 per SM
+        int64_t grid = want < cap ? want : cap;
+        if (grid >= num_sms) grid = (grid / num_sms) * num_sms;   // whole waves
+        if (grid < 1) grid = 1;
+        reshape_and_cache_vec16_kernel<kUnroll><<<(unsigned)grid, threads, 0, stream>>>(
+            static_cast<const uint8_t *>(a.key), static_cast<const uint8_t *>(a.value),
+            a.slot_mapping, static_cast<uint8_t *>(a.key_cache),
+            static_cast<uint8_t *>(a.value_cache), total, vecs_per_head, a.num_kv_heads,
+            a.block_size, num_slots, a.key_stride * eb, a.value_stride * eb,
+            a.block_stride * eb, a.head_stride * eb, a.entry_stride * eb);
+    } else {
+        const int64_t total = (int64_t)a.num_tokens * a.num_kv_heads * a.size_per_head;
+        int64_t grid = (total + 255) / 256;
+        const int64_t cap = (int64_t)num_sms * 8;
+        if (grid > cap) grid = cap;
+        reshape_and_cache_u16_kernel<<<(unsigned)grid, 256, 0, stream>>>(
+            static_cast<const uint16_t *>(a.key), static_cast<const uint16_t *>(a.value),
+            a.slot_mapping, static_cast<uint16_t *>(a.key_cache),
+            static_cast<uint16_t *>(a.value_cache), total, a.size_per_head, a.num_kv_heads,
+            a.block_size, num_slots, a.key_stride, a.value_stride, a.block_stride,
+            a.head_stride, a.entry_stride);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace kern
+}  // namespace tecoops

@@ -1,0 +1,130 @@
+// Branch selection, workspace sizing and launch bridges of the flash_attention
+// UAL operator (reference teco/ual/ops/flash_attention/find_flash_attention.cpp:39-43).
+#include "ual/ops/flash_attention.hpp"
+
+#include <cmath>
+
+#include "ual/kernels/launchers.h"
+
+namespace tecoops {
+namespace ual {
+namespace ops {
+
+using args::ElemType;
+using args::FlashAttentionArgs;
+
+static kern::AttnShape toShape(const FlashAttentionArgs &a) {
+    kern::AttnShape s;
+    s.q = a.q;
+    s.key_cache = a.key_cache;
+    s.value_cache = a.value_cache;
+    s.out = a.fmha_out;
+    s.q_seq_lens = a.q_seq_lens;
+    s.kv_seq_lens = a.kv_seq_lens;
+    s.block_table = a.block_table;
+    s.batch = a.batch_size;
+    s.num_heads = a.local_head_num;
+    s.num_kv_heads = a.local_kv_head_num;
+    s.head_dim = a.size_per_head;
+    s.block_size = a.block_size;
+    s.block_table_dim = a.block_table_dim;
+    s.num_pages = a.max_block_num;
+    s.total_q = a.total_q;
+    s.max_q = a.max_q_seq_len;
+    s.max_k = a.max_k_seq_len;
+    s.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    return s;
+}
+
+static void decodePlan(const FlashAttentionArgs &a, int *split, int *max_splits) {
+    kern::decode_plan(a.num_sms, a.batch_size, a.local_kv_head_num,
+                      a.local_head_num / a.local_kv_head_num, a.max_k_seq_len, split, max_splits);
+}
+
+static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
+    kern::DecodeParams p;
+    p.q = a.q;
+    p.key_cache = a.key_cache;
+    p.value_cache = a.value_cache;
+    p.out = a.fmha_out;
+    p.q_seq_lens = a.q_seq_lens;
+    p.kv_seq_lens = a.kv_seq_lens;
+    p.block_table = a.block_table;
+    p.batch = a.batch_size;
+    p.num_heads = a.local_head_num;
+    p.num_kv_heads = a.local_kv_head_num;
+    p.group = a.local_head_num / a.local_kv_head_num;
+    p.num_slices = (p.group + 15) / 16;
+    p.head_dim = a.size_per_head;
+    p.block_size = a.block_size;
+    p.block_table_dim = a.block_table_dim;
+    decodePlan(a, &p.split_tokens, &p.max_splits);
+    p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    p.part_o = nullptr;
+    p.part_lse = nullptr;
+    if (p.max_splits > 1) {
+        const size_t need = kern::decode_workspace_bytes(p.batch, p.num_heads, p.head_dim,
+                                                         p.max_splits);
+        if (a.workspace == nullptr || a.workspace_bytes < need) return cudaErrorInvalidValue;
+        const size_t recs = (size_t)p.batch * p.num_heads * p.max_splits;
+        p.part_o = static_cast<float *>(a.workspace);
+        p.part_lse = p.part_o + recs * p.head_dim;
+    }
+    return kern::launch_decode(p, a.dtype == ElemType::BF16, stream);
+}
+
+static cudaError_t runPrefill(const FlashAttentionArgs &a, cudaStream_t stream) {
+    return kern::launch_prefill(toShape(a), a.dtype == ElemType::BF16, a.workspace, a.dev_error,
+                                a.num_sms, stream);
+}
+
+static cudaError_t runGeneric(const FlashAttentionArgs &a, cudaStream_t stream) {
+    return kern::launch_generic_attention(toShape(a), a.dtype == ElemType::BF16, stream);
+}
+
+FlashAttentionAlgos FlashAttentionOp::selectAlgo(const FlashAttentionArgs &a) {
+    const int group = a.local_head_num / a.local_kv_head_num;
+    if (a.max_q_seq_len == 1 && kern::decode_supported(a.size_per_head, a.block_size, group))
+        return FlashAttentionAlgos::DECODE_SPLITKV;
+    if (kern::prefill_supported(a.size_per_head, a.block_size, group))
+        return FlashAttentionAlgos::PREFILL_TCGEN05;
+    return FlashAttentionAlgos::GENERIC;
+}
+
+size_t FlashAttentionOp::workspaceSize(const FlashAttentionArgs &a) {
+    switch (selectAlgo(a)) {
+        case FlashAttentionAlgos::DECODE_SPLITKV: {
+            int split = 0, ms = 0;
+            decodePlan(a, &split, &ms);
+            return kern::decode_workspace_bytes(a.batch_size, a.local_head_num, a.size_per_head,
+                                                ms);
+        }
+        case FlashAttentionAlgos::PREFILL_TCGEN05:
+            return kern::prefill_workspace_bytes(toShape(a));
+        default:
+            return 0;
+    }
+}
+
+Status FlashAttentionOp::findImpl(const args::FlashAttentionPatchArgs *p) {
+    if (p == nullptr || p->rvargs == nullptr) return Status::BAD_PARAMETER;
+    const FlashAttentionArgs &a = *p->rvargs;
+    if (a.size_per_head > 256) return Status::NOT_IMPLEMENTED;
+    algo_ = selectAlgo(a);
+    switch (algo_) {
+        case FlashAttentionAlgos::DECODE_SPLITKV:
+            setInstance(&runDecode, "fa_decode_splitkv_sm100");
+            break;
+        case FlashAttentionAlgos::PREFILL_TCGEN05:
+            setInstance(&runPrefill, "fa_prefill_tcgen05_sm100");
+            break;
+        default:
+            setInstance(&runGeneric, "fa_generic_sm100");
+            break;
+    }
+    return Status::SUCCESS;
+}
+
+}  // namespace ops
+}  // namespace ual
+}  // namespace tecoops

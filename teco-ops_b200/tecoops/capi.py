@@ -1,0 +1,166 @@
+"""ctypes binding of the C ABI in include/tecoops.h (libteco_ops.so).
+
+This is the binding a Python caller without the torch extension would use: plain
+pointers and sizes, statuses returned as ints.  The parity tests call the
+kernels through it.  Device pointers are plain integers (e.g. ``tensor.data_ptr()``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY_PATH = os.path.join(_HERE, "libteco_ops.so")
+
+# tecoopsStatus_t
+SUCCESS, NOT_INITIALIZED, ALLOC_FAILED, BAD_PARAM, INTERNAL_ERROR, INVALID_VALUE, \
+    NOT_SUPPORTED = range(7)
+# tecoopsDataType_t
+DATA_FLOAT, DATA_HALF, DATA_INT8, DATA_INT16, DATA_INT32, DATA_INT64, DATA_UINT8, DATA_BOOL, \
+    DATA_DOUBLE, DATA_BFLOAT16, DATA_COMPLEX_FLOAT = range(11)
+# tecoopsTensorFormat_t
+TENSOR_NCHW, TENSOR_NHWC, TENSOR_CHWN, TENSOR_NWHC = range(4)
+
+# every symbol declared in include/tecoops.h
+EXPORTED = [
+    "tecoopsCreate", "tecoopsDestroy", "tecoopsSetStream", "tecoopsGetStream",
+    "tecoopsGetErrorString", "tecoopsCreateTensorDescriptor", "tecoopsSetTensor4dDescriptor",
+    "tecoopsGetTensor4dDescriptor", "tecoopsSetTensorNdDescriptor",
+    "tecoopsGetTensorNdDescriptor", "tecoopsDestroyTensorDescriptor", "tecoopsMemset",
+    "tecoopsReshapeAndCache", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
+    "tecoopsGetDeviceErrorStatus", "tecoopsFlattenRays", "tecoopsReduceVariance",
+    "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsCausalConv1d",
+]
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_lib = None
+
+
+class TecoopsError(RuntimeError):
+    def __init__(self, what: str, status: int):
+        super().__init__(f"{what}: {error_string(status)} ({status})")
+        self.status = status
+
+
+def lib():
+    """Load libteco_ops.so (raises OSError loudly when it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIBRARY_PATH):
+        raise OSError(f"libteco_ops.so not built at {LIBRARY_PATH}; run teco-ops_b200/build.py")
+    L = ctypes.CDLL(LIBRARY_PATH)
+    sig = {
+        "tecoopsCreate": [ctypes.POINTER(_vp)],
+        "tecoopsDestroy": [_vp],
+        "tecoopsSetStream": [_vp, _vp],
+        "tecoopsGetStream": [_vp, ctypes.POINTER(_vp)],
+        "tecoopsCreateTensorDescriptor": [ctypes.POINTER(_vp)],
+        "tecoopsSetTensor4dDescriptor": [_vp, _i, _i, _i, _i, _i, _i],
+        "tecoopsGetTensor4dDescriptor": [_vp] + [ctypes.POINTER(_i)] * 9,
+        "tecoopsSetTensorNdDescriptor": [_vp, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)],
+        "tecoopsGetTensorNdDescriptor": [_vp, _i, ctypes.POINTER(_i), ctypes.POINTER(_i),
+                                         ctypes.POINTER(_i), ctypes.POINTER(_i)],
+        "tecoopsDestroyTensorDescriptor": [_vp],
+        "tecoopsMemset": [_vp, _vp, _i, ctypes.c_size_t],
+        "tecoopsReshapeAndCache": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i],
+        "tecoopsFlashAttention": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                  _vp, _vp, _vp, _vp],
+        "tecoopsGetFlashAttentionWorkspaceSize": [_vp, _i, _i, _vp, _vp, _vp,
+                                                  ctypes.POINTER(ctypes.c_size_t)],
+        "tecoopsGetDeviceErrorStatus": [_vp, ctypes.POINTER(_i)],
+        "tecoopsRmsNorm": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float],
+    }
+    for name, args in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = _i
+    L.tecoopsGetErrorString.argtypes = [_i]
+    L.tecoopsGetErrorString.restype = ctypes.c_char_p
+    _lib = L
+    return L
+
+
+def error_string(status: int) -> str:
+    return lib().tecoopsGetErrorString(int(status)).decode()
+
+
+def check(status: int, what: str):
+    if status != SUCCESS:
+        raise TecoopsError(what, status)
+
+
+class Handle:
+    """Owns a tecoopsHandle_t (created on the current CUDA device)."""
+
+    def __init__(self, stream: int = 0):
+        self.h = _vp()
+        check(lib().tecoopsCreate(ctypes.byref(self.h)), "tecoopsCreate")
+        if stream:
+            check(lib().tecoopsSetStream(self.h, _vp(stream)), "tecoopsSetStream")
+
+    def set_stream(self, stream: int):
+        check(lib().tecoopsSetStream(self.h, _vp(stream)), "tecoopsSetStream")
+
+    def close(self):
+        if self.h:
+            lib().tecoopsDestroy(self.h)
+            self.h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Desc:
+    """Owns a tecoopsTensorDescriptor_t set with packed Nd dims."""
+
+    def __init__(self, dtype: int, dims):
+        self.d = _vp()
+        check(lib().tecoopsCreateTensorDescriptor(ctypes.byref(self.d)), "CreateTensorDescriptor")
+        arr = (_i * len(dims))(*[int(x) for x in dims])
+        check(lib().tecoopsSetTensorNdDescriptor(self.d, dtype, len(dims), arr, None),
+              "SetTensorNdDescriptor")
+
+    def __del__(self):
+        try:
+            lib().tecoopsDestroyTensorDescriptor(self.d)
+        except Exception:
+            pass
+
+
+def reshape_and_cache(handle: Handle, key, value, slot_mapping, key_cache, value_cache,
+                      num_tokens, num_kv_heads, head_size, num_blocks, block_size) -> int:
+    """Raw C call; pointers are ints. Returns the tecoopsStatus_t."""
+    return lib().tecoopsReshapeAndCache(handle.h, _vp(key), _vp(value), _vp(slot_mapping),
+                                        _vp(key_cache), _vp(value_cache), num_tokens,
+                                        num_kv_heads, head_size, num_blocks, block_size)
+
+
+def flash_attention(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num, q_seq_lens,
+                    kv_seq_lens, bt_desc: Desc, block_table, q_desc: Desc, q, k_desc: Desc,
+                    k_cache, v_desc: Desc, v_cache, o_desc: Desc, out, workspace=0) -> int:
+    return lib().tecoopsFlashAttention(handle.h, max_seqlen_q, max_seqlen_k, max_block_num,
+                                       _vp(q_seq_lens), _vp(kv_seq_lens), bt_desc.d,
+                                       _vp(block_table), q_desc.d, _vp(q), k_desc.d,
+                                       _vp(k_cache), v_desc.d, _vp(v_cache), o_desc.d, _vp(out),
+                                       _vp(workspace) if workspace else None)
+
+
+def workspace_size(handle: Handle, max_seqlen_q, max_seqlen_k, bt_desc: Desc, q_desc: Desc,
+                   k_desc: Desc) -> int:
+    n = ctypes.c_size_t(0)
+    check(lib().tecoopsGetFlashAttentionWorkspaceSize(handle.h, max_seqlen_q, max_seqlen_k,
+                                                      bt_desc.d, q_desc.d, k_desc.d,
+                                                      ctypes.byref(n)),
+          "GetFlashAttentionWorkspaceSize")
+    return n.value
+
+
+def device_error(handle: Handle):
+    code = _i(0)
+    st = lib().tecoopsGetDeviceErrorStatus(handle.h, ctypes.byref(code))
+    return st, code.value

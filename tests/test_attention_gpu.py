@@ -1,0 +1,153 @@
+"""flash_attention on the GPU through the C ABI against the oracle and the
+reference golden (fixture samples).  Tolerances (north star): max-abs <= 2e-2
+and mean-abs <= 2e-3 against the fp32 golden; the zoo's DIFF1 <= 1e-2 too."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from oracle import seeded
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+DIFF1 = 1e-2
+
+
+@pytest.fixture(autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _run_case(c):
+    from gpu_util import attention_capi, attn_case_to_dev
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    out = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"])
+    torch.cuda.synchronize()
+    return inp, out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("name", sorted(cases.ATTN_CASES))
+def test_attention_vs_oracle_and_golden(golden, name):
+    from gpu_util import errors
+    c = cases.ATTN_CASES[name]
+    inp, out = _run_case(c)
+    ref = oracle.flash_attn_varlen(
+        seeded.words_to_f32(inp["q"], c["dtype"]), seeded.words_to_f32(inp["k_cache"], c["dtype"]),
+        seeded.words_to_f32(inp["v_cache"], c["dtype"]), inp["q_lens"], inp["kv_lens"],
+        inp["block_table"])
+    assert np.isfinite(out).all()
+    mx, mean, diff1 = errors(out, ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS and diff1 <= DIFF1, (mx, mean, diff1)
+    idx = golden[f"attn/{name}/idx"]
+    gmx, gmean, _ = errors(out.reshape(-1)[idx], golden[f"attn/{name}/val"])
+    assert gmx <= MAX_ABS and gmean <= MEAN_ABS, (gmx, gmean)
+
+
+def test_attention_deterministic():
+    c = cases.ATTN_CASES["bf16_bs16_varlen"]
+    _, a = _run_case(c)
+    _, b = _run_case(c)
+    assert np.array_equal(a, b)
+
+
+def _config2_inputs(seed=10):
+    """4 seqs, L ~ U{512..2048}, Hq 32, Hkv 8, D 128, bf16, bs 16,
+    contiguous pages, K/V written by reshape_and_cache first."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    lens = torch.randint(512, 2049, (4,), generator=g).tolist()
+    return lens
+
+
+def test_config2_prefill_full_size():
+    from gpu_util import attention_capi, errors, reshape_capi
+    lens = _config2_inputs()
+    Hq, Hkv, D, bs = 32, 8, 128, 16
+    tot = sum(lens)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q = torch.randn(tot, Hq, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    k = torch.randn(tot, Hkv, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    v = torch.randn(tot, Hkv, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    pages = [(l + bs - 1) // bs for l in lens]
+    NB = sum(pages)
+    bt = torch.zeros(4, max(pages), dtype=torch.int32)
+    slot = []
+    p0 = 0
+    for b, l in enumerate(lens):
+        bt[b, :pages[b]] = torch.arange(p0, p0 + pages[b], dtype=torch.int32)
+        slot.append(torch.arange(l) + p0 * bs)
+        p0 += pages[b]
+    slot = torch.cat(slot).cuda()
+    kc = torch.zeros(NB, Hkv, bs, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    reshape_capi(k, v, slot, kc, vc)
+    ql = torch.tensor(lens, dtype=torch.int32).cuda()
+    out = attention_capi(q, kc, vc, ql, ql, bt.cuda())
+    torch.cuda.synchronize()
+    ref = oracle.flash_attn_varlen(q.float().cpu().numpy(), kc.float().cpu().numpy(),
+                                   vc.float().cpu().numpy(), lens, lens, bt.numpy())
+    mx, mean, diff1 = errors(out.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS and diff1 <= DIFF1, (mx, mean, diff1)
+
+
+def test_config3_decode_full_size():
+    """64 seqs, context U{512..8192}, 40,000-page pool with a
+    random permutation, bs 16, Hq 32, Hkv 8, D 128, bf16."""
+    from gpu_util import attention_capi, errors
+    B, Hq, Hkv, D, bs, pool = 64, 32, 8, 128, 16, 40000
+    g = torch.Generator(device="cpu").manual_seed(20)
+    ctx = torch.randint(512, 8193, (B,), generator=g)
+    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(21)).to(torch.int32)
+    pages = ((ctx + bs - 1) // bs).tolist()
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    p0 = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[p0:p0 + pages[b]]
+        p0 += pages[b]
+    gd = torch.Generator(device="cuda").manual_seed(22)
+    kc = torch.randn(pool, Hkv, bs, D, device="cuda", dtype=torch.bfloat16, generator=gd)
+    vc = torch.randn(pool, Hkv, bs, D, device="cuda", dtype=torch.bfloat16, generator=gd)
+    q = torch.randn(B, Hq, D, device="cuda", dtype=torch.bfloat16, generator=gd)
+    ones = torch.ones(B, dtype=torch.int32, device="cuda")
+    out = attention_capi(q, kc, vc, ones, ctx.to(torch.int32).cuda(), bt.cuda(), max_q=1,
+                         max_k=int(ctx.max()))
+    torch.cuda.synchronize()
+    # oracle on a compacted pool (only the pages the block tables use)
+    used = torch.unique(bt[bt >= 0]).long()
+    remap = torch.full((pool,), -1, dtype=torch.int32)
+    remap[used] = torch.arange(used.numel(), dtype=torch.int32)
+    kcc = kc[used.cuda()].float().cpu().numpy()
+    vcc = vc[used.cuda()].float().cpu().numpy()
+    btc = remap[bt.long()].numpy()
+    ref = oracle.flash_attn_varlen(q.float().cpu().numpy(), kcc, vcc, [1] * B, ctx.tolist(), btc)
+    mx, mean, diff1 = errors(out.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS and diff1 <= DIFF1, (mx, mean, diff1)
+
+
+def test_decode_caller_workspace_matches_handle_scratch():
+    from gpu_util import attention_capi, attn_case_to_dev, handle
+    from tecoops import capi
+    c = cases.ATTN_CASES["bf16_bs16_decode"]
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, "bf16")
+    a = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"])
+    dt = capi.DATA_BFLOAT16
+    ws = capi.workspace_size(handle(), 1, int(inp["kv_lens"].max()),
+                             capi.Desc(capi.DATA_INT32, d["bt"].shape), capi.Desc(dt, d["q"].shape),
+                             capi.Desc(dt, d["kc"].shape))
+    buf = torch.empty(max(ws, 16), dtype=torch.uint8, device="cuda")
+    b = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"],
+                       workspace=buf.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_no_device_errors_recorded():
+    from gpu_util import handle
+    from tecoops import capi
+    st, code = capi.device_error(handle())
+    assert st == capi.SUCCESS and code == 0

@@ -1,0 +1,90 @@
+"""The PyTorch binding keeps the reference's Python surface
+(api/torch_ext.cpp:208-215, called as in python_api_test/test_flash_attention.py:203-216
+and python_api_test/test_reshape_and_cache.py:105-110) and the TORCH_LIBRARY ops."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from oracle import seeded
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def test_reshape_and_cache_binding_matches_golden(golden):
+    import hashlib
+
+    import tecoops
+    from gpu_util import dev_to_words, words_to_dev
+    c = cases.RESHAPE_CASES["cfg1_fp16"]
+    key, value, slot, kc, vc = cases.reshape_inputs(c)
+    dkc, dvc = words_to_dev(kc, "f16"), words_to_dev(vc, "f16")
+    tecoops.reshape_and_cache(words_to_dev(key, "f16"), words_to_dev(value, "f16"),
+                              torch.from_numpy(slot).cuda(), dkc, dvc)
+    torch.cuda.synchronize()
+    assert hashlib.sha256(dev_to_words(dkc).tobytes()).digest() == bytes(golden["rc/cfg1_fp16/sha_k"])
+    assert hashlib.sha256(dev_to_words(dvc).tobytes()).digest() == bytes(golden["rc/cfg1_fp16/sha_v"])
+
+
+@pytest.mark.parametrize("name", ["api_mix_decode_prefill", "api_decode_2x128", "bf16_bs16_varlen"])
+def test_flash_attn_varlen_func_reference_signature(name):
+    import tecoops
+    from gpu_util import attention_capi, attn_case_to_dev, errors
+    c = cases.ATTN_CASES[name]
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    ql = inp["q_lens"]
+    cu = torch.zeros(len(ql) + 1, dtype=torch.int32)
+    cu[1:] = torch.from_numpy(np.cumsum(ql)).to(torch.int32)
+    out = torch.empty_like(d["q"])
+    tecoops.flash_attn_varlen_func(
+        d["q"], d["kc"], d["vc"], int(ql.max()), cu.cuda(), int(inp["kv_lens"].max()),
+        torch.Tensor(), d["kv_lens"], 1.0 / np.sqrt(c["D"]), True, torch.Tensor(), d["bt"],
+        False, out)
+    ref_capi = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"])
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_capi)
+    ref = oracle.flash_attn_varlen(
+        seeded.words_to_f32(inp["q"], c["dtype"]), seeded.words_to_f32(inp["k_cache"], c["dtype"]),
+        seeded.words_to_f32(inp["v_cache"], c["dtype"]), inp["q_lens"], inp["kv_lens"],
+        inp["block_table"])
+    mx, mean, _ = errors(out.float().cpu().numpy(), ref)
+    assert mx <= 2e-2 and mean <= 2e-3
+
+
+def test_torch_library_ops():
+    import tecoops  # noqa: F401  (registers torch.ops.tecoops)
+    from gpu_util import attention_capi, attn_case_to_dev
+    c = cases.ATTN_CASES["api_chunked_2b"]
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    out = torch.empty_like(d["q"])
+    torch.ops.tecoops.flash_attention(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"],
+                                      int(inp["q_lens"].max()), int(inp["kv_lens"].max()), out)
+    ref = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"])
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    key = torch.randn(8, 2, 64, device="cuda", dtype=torch.bfloat16)
+    kc = torch.zeros(4, 2, 16, 64, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slot = torch.tensor([0, 17, -1, 5, 63, 32, 1, 2], device="cuda")
+    torch.ops.tecoops.reshape_and_cache(key, key, slot, kc, vc)
+    torch.cuda.synchronize()
+    assert torch.equal(kc[1, :, 1], key[1]) and torch.equal(vc[3, :, 15], key[4])
+
+
+def test_binding_rejects_cpu_tensors():
+    import tecoops
+    with pytest.raises(RuntimeError):
+        tecoops.reshape_and_cache(torch.zeros(1, 1, 8, dtype=torch.half),
+                                  torch.zeros(1, 1, 8, dtype=torch.half),
+                                  torch.zeros(1, dtype=torch.long),
+                                  torch.zeros(1, 1, 16, 8, dtype=torch.half),
+                                  torch.zeros(1, 1, 16, 8, dtype=torch.half))

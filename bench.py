@@ -320,6 +320,9 @@ def run_ours(args):
     W = Workloads(rank)
     W.set_stream()
     peaks, peak_src = load_peaks()
+    if args.only:
+        run_only(W, args, torch, rank)
+        return
 
     def barrier():
         if world > 1:
@@ -417,6 +420,20 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_only(W, args, torch, rank):
+    """One workload's timed loop (profiler captures run this)."""
+    if args.only == "prefill":
+        ph, fl = [W.reshape2, W.prefill2], W.flush
+    elif args.only == "decode":
+        W.setup_decode(rank)
+        ph, fl = [W.decode_step, W.decode_attn], None
+    else:
+        W.setup_reshape(rank)
+        ph, fl = [W.reshape4], None
+    t = timed_loop(torch, args.steps, args.warmup, ph, flush=fl)
+    print(json.dumps({"only": args.only, "ms_per_phase": [sum(x) / len(x) for x in t]}))
 
 
 def run_e2e(W, args, torch, world, max_over_ranks, barrier):
@@ -538,6 +555,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--only", choices=["prefill", "decode", "reshape"], default=None,
+                    help="run one workload's timed loop only (for profiler captures); "
+                         "prints a reduced JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -77,6 +77,7 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_splitkv_kernel(DecodePa
     if (kv_begin >= kv_len && !(split == 0 && kv_len <= 0)) return;
     const int kv_end = min(kv_len, kv_begin + p.split_tokens);
     const int qrow = warp_seq_start(p.q_seq_lens, b);   // q_len == 1 on this path
+    if (qrow >= p.total_q) return;                      // lengths beyond q's rows
 
     const int head0 = kvh * p.group + slice * 16;              // first q head of this tile
     const int rows = min(16, p.group - slice * 16);            // valid q heads
@@ -120,10 +121,11 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_splitkv_kernel(DecodePa
             const int r = id / kChunks;
             const int ch = id - r * kChunks;
             const int tok = t0 + r;
-            const bool valid = tok < kv_end;
+            bool valid = tok < kv_end;
             int64_t off = 0;
+            int blk = valid ? __ldg(bt + tok / p.block_size) : -1;
+            valid = valid && blk >= 0 && blk < p.num_pages;   // bad page ids read as zeros
             if (valid) {
-                const int blk = __ldg(bt + tok / p.block_size);
                 const int in_page = tok - (tok / p.block_size) * p.block_size;
                 off = (int64_t)blk * page_stride + head_off + (int64_t)in_page * D + ch * 8;
             }
@@ -296,6 +298,7 @@ __global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
     const int ns = (kv_len + p.split_tokens - 1) / p.split_tokens;
     if (q_len <= 0 || ns <= 1) return;
     const int qrow = warp_seq_start(p.q_seq_lens, b);
+    if (qrow >= p.total_q) return;
     const int64_t rec0 = ((int64_t)b * p.num_heads + h) * p.max_splits;
     float M = -INFINITY;
     for (int s = 0; s < ns; ++s) M = fmaxf(M, p.part_lse[rec0 + s]);

@@ -71,7 +71,8 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
         float x = -INFINITY;
         int64_t my_off = 0;
         if (j < allowed) {
-            const int blk = __ldg(bt + j / s.block_size);
+            int blk = __ldg(bt + j / s.block_size);
+            if (blk < 0 || blk >= s.num_pages) blk = 0;   // bad page id: stay in bounds
             my_off = (int64_t)blk * page_stride + head_off + (int64_t)(j % s.block_size) * D;
             float dot = 0.f;
             for (int d = 0; d < D; ++d) dot += qs[warp][d] * Elem<T>::to_float(kc[my_off + d]);

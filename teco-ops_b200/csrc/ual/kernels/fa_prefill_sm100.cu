@@ -78,6 +78,7 @@ struct PrefillParams {
     int block_table_dim;
     int num_pages;
     int num_qtiles;     // ceil(max_q / 128)
+    int total_q;
     float scale_log2;
 };
 
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (warp >= 4) {
             const int r = threadIdx.x - 128;
             const int qs = warp_seq_start(p.q_seq_lens, b);
-            if (r < rows_valid) {
+            if (r < rows_valid && qs + q0 + r < p.total_q) {
                 T *o = static_cast<T *>(p.out) + ((int64_t)(qs + q0 + r) * p.num_heads + h) * D;
                 for (int d = 0; d < D; ++d) o[d] = Elem<T>::from_float(0.f);
             }
@@ -401,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t u[32];
                 tmem_ld32(tmem + lane_addr + kColO + c * 32, u);
                 tmem_ld_wait();
-                if (r < rows_valid) {
+                if (r < rows_valid && qs + qi < p.total_q) {
                     uint32_t pkd[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
@@ -510,6 +511,7 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, cudaStre
     p.block_table_dim = s.block_table_dim;
     p.num_pages = s.num_pages;
     p.num_qtiles = (s.max_q + kBM - 1) / kBM;
+    p.total_q = s.total_q;
     p.scale_log2 = s.scale_log2;
     if (p.num_qtiles <= 0 || s.batch <= 0) return cudaSuccess;
 

@@ -57,6 +57,8 @@ struct DecodeParams {
     int head_dim;
     int block_size;
     int block_table_dim;
+    int num_pages;      // pages in the cache pool (ids outside read as zeros)
+    int total_q;        // rows of q / out
     int split_tokens;   // multiple of 64
     int max_splits;
     float scale_log2;

@@ -58,6 +58,8 @@ static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
     p.head_dim = a.size_per_head;
     p.block_size = a.block_size;
     p.block_table_dim = a.block_table_dim;
+    p.num_pages = a.max_block_num;
+    p.total_q = a.total_q;
     decodePlan(a, &p.split_tokens, &p.max_splits);
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
     p.part_o = nullptr;

@@ -180,6 +180,33 @@ tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(tecoopsHandle_t handle,
                                                       size_t *workspace_bytes);
 
 /*
+ * Extension with no counterpart in the reference: the split-KV decode of
+ * tecoopsFlashAttention (every q_len 0 or 1) for callers that cannot allocate
+ * device memory, such as an engine plugin that is handed only its input and
+ * output buffers, or a server whose memory planner forbids allocations after
+ * start-up.  It allocates nothing: the split scratch is a static 16 MiB device
+ * array inside the library (held by every GPU that loads the library until
+ * exit); shapes whose split plan needs more than 16 MiB are rejected with
+ * TECOOPS_STATUS_NOT_SUPPORTED.  The first call on a device looks up the
+ * array's device address, so make it before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race and must be serialised.
+ * Arguments as tecoopsFlashAttention (max_seqlen_q is implicitly 1, no
+ * workspace); results are identical to it for the same inputs.
+ */
+tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(tecoopsHandle_t handle, int max_seqlen_k,
+                                                   const int *q_seq_lens, const int *kv_seq_lens,
+                                                   const tecoopsTensorDescriptor_t blockTableDesc,
+                                                   const void *blockTable,
+                                                   const tecoopsTensorDescriptor_t qDataDesc,
+                                                   const void *qData,
+                                                   const tecoopsTensorDescriptor_t kCacheDesc,
+                                                   const void *kCache,
+                                                   const tecoopsTensorDescriptor_t vCacheDesc,
+                                                   const void *vCache,
+                                                   const tecoopsTensorDescriptor_t oDataDesc,
+                                                   void *oData);
+
+/*
  * Extension: status of the last device-side check of this handle's stream
  * (bounded waits that gave up).  Synchronises the handle's stream.
  * Returns TECOOPS_STATUS_INTERNAL_ERROR if a kernel reported an error since the

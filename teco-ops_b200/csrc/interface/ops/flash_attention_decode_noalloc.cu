@@ -1,0 +1,166 @@
+// tecoopsFlashAttentionDecodeNoAlloc: the split-KV decode path for callers that
+// cannot allocate device memory.
+//
+// Some callers cannot call cudaMalloc at the point where they run attention.
+// One example is an inference-engine plugin whose Enqueue receives only the
+// input and output buffers from the engine (the reference's plugin passes
+// workspace = nullptr).  Another is a serving loop whose memory planner forbids
+// allocations after start-up, because cudaMalloc synchronises the device and can
+// fail once the pool is carved up.  tecoopsFlashAttention would then fall back
+// to the handle's lazily grown scratch, and that fallback calls cudaMalloc.
+//
+// This entry point runs the same split-KV decode kernels with the same split
+// plan.  Its scratch (the per-split partial outputs and log-sum-exp values) lives
+// in a file-scope __device__ array of kNoAllocScratchBytes (16 MiB).  Every GPU
+// that loads this library holds that array until the process exits.
+//
+// Host code cannot use the array's name as a device address: in host code the
+// symbol is only a stand-in.  So the array's device address is looked up with
+// cudaGetSymbolAddress, once per device with that device current, on the first
+// call made on that device.  Make that first call before any stream capture.
+//
+// All calls share the one array, and it keeps the contents of the last call.
+// Nothing in it needs to start at zero: every partial is written before it is
+// read within the same call.  Calls that overlap on the GPU (for example on two
+// streams of one device at once) race on the array; serialise them.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <mutex>
+
+#include "interface/common/context.h"
+#include "tecoops.h"
+#include "ual/com/log.h"
+#include "ual/kernels/launchers.h"
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;   // 16 MiB per device
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+std::mutex g_setup_mutex;
+void *g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_decode_scratch on `device` (which must be current).
+// Looked up once per device; returns nullptr if the lookup fails.
+void *scratchFor(int device) {
+    if (device < 0 || device >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (g_scratch_ptr[device] == nullptr) {
+        void *ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+        if (e != cudaSuccess) {
+            TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: cudaGetSymbolAddress failed on device "
+                       "%d: %s",
+                       device, cudaGetErrorString(e));
+            cudaGetLastError();
+            return nullptr;
+        }
+        g_scratch_ptr[device] = ptr;
+    }
+    return g_scratch_ptr[device];
+}
+
+bool packedDesc(const tecoopsTensorStruct *d) {
+    int s = 1;
+    for (int i = d->nbDims - 1; i >= 0; --i) {
+        if (d->strideA[i] != s) return false;
+        s *= d->dimA[i];
+    }
+    return true;
+}
+
+}  // namespace
+
+extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
+    tecoopsHandle_t handle, int max_seqlen_k, const int *q_seq_lens, const int *kv_seq_lens,
+    const tecoopsTensorDescriptor_t blockTableDesc, const void *blockTable,
+    const tecoopsTensorDescriptor_t qDataDesc, const void *qData,
+    const tecoopsTensorDescriptor_t kCacheDesc, const void *kCache,
+    const tecoopsTensorDescriptor_t vCacheDesc, const void *vCache,
+    const tecoopsTensorDescriptor_t oDataDesc, void *oData) {
+    if (handle == nullptr) return TECOOPS_STATUS_NOT_INITIALIZED;
+    const tecoopsTensorStruct *bt = blockTableDesc, *q = qDataDesc, *k = kCacheDesc,
+                              *v = vCacheDesc, *o = oDataDesc;
+    if (!bt || !q || !k || !v || !o || !q_seq_lens || !kv_seq_lens || !blockTable || !qData ||
+        !kCache || !vCache || !oData || max_seqlen_k < 0)
+        return TECOOPS_STATUS_BAD_PARAM;
+    if (k->dataType != v->dataType ||
+        (k->dataType != TECOOPS_DATA_HALF && k->dataType != TECOOPS_DATA_BFLOAT16) ||
+        q->dataType != k->dataType || o->dataType != k->dataType ||
+        bt->dataType != TECOOPS_DATA_INT32)
+        return TECOOPS_STATUS_BAD_PARAM;
+    if (k->nbDims != 4 || v->nbDims != 4 || q->nbDims != 3 || o->nbDims != 3 || bt->nbDims != 2)
+        return TECOOPS_STATUS_BAD_PARAM;
+    for (int i = 0; i < 4; ++i)
+        if (k->dimA[i] != v->dimA[i]) return TECOOPS_STATUS_BAD_PARAM;
+    for (int i = 0; i < 3; ++i)
+        if (q->dimA[i] != o->dimA[i]) return TECOOPS_STATUS_BAD_PARAM;
+    if (q->dimA[2] != k->dimA[3] || q->dimA[1] <= 0 || k->dimA[1] <= 0 ||
+        q->dimA[1] % k->dimA[1] != 0 || bt->dimA[0] <= 0 || bt->dimA[1] <= 0 ||
+        k->dimA[0] <= 0 || k->dimA[2] <= 0)
+        return TECOOPS_STATUS_BAD_PARAM;
+    if (!packedDesc(q) || !packedDesc(o) || !packedDesc(k) || !packedDesc(v) || !packedDesc(bt))
+        return TECOOPS_STATUS_NOT_SUPPORTED;
+    const int batch = bt->dimA[0], heads = q->dimA[1], kv_heads = k->dimA[1];
+    const int head_dim = q->dimA[2], block_size = k->dimA[2];
+    const int group = heads / kv_heads;
+    if (!tecoops::kern::decode_supported(head_dim, block_size, group)) {
+        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: head_dim %d / block_size %d not covered "
+                   "by the split-KV decode kernel",
+                   head_dim, block_size);
+        return TECOOPS_STATUS_NOT_SUPPORTED;
+    }
+    if (q->dimA[0] == 0) return TECOOPS_STATUS_SUCCESS;
+
+    tecoops::kern::DecodeParams p;
+    p.q = qData;
+    p.key_cache = kCache;
+    p.value_cache = vCache;
+    p.out = oData;
+    p.q_seq_lens = q_seq_lens;
+    p.kv_seq_lens = kv_seq_lens;
+    p.block_table = static_cast<const int *>(blockTable);
+    p.batch = batch;
+    p.num_heads = heads;
+    p.num_kv_heads = kv_heads;
+    p.group = group;
+    p.num_slices = (group + 15) / 16;
+    p.head_dim = head_dim;
+    p.block_size = block_size;
+    p.block_table_dim = bt->dimA[1];
+    p.num_pages = k->dimA[0];
+    p.total_q = q->dimA[0];
+    tecoops::kern::decode_plan(handle->num_sms, batch, kv_heads, group, max_seqlen_k,
+                               &p.split_tokens, &p.max_splits);
+    p.scale_log2 = (float)(1.0 / std::sqrt((double)head_dim)) * 1.4426950408889634f;
+    p.part_o = nullptr;
+    p.part_lse = nullptr;
+    const size_t need =
+        tecoops::kern::decode_workspace_bytes(batch, heads, head_dim, p.max_splits);
+    if (need > kNoAllocScratchBytes) {
+        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: these shapes need %zu bytes of split "
+                   "scratch; the static scratch holds %zu bytes (16 MiB). Use "
+                   "tecoopsFlashAttention with a workspace instead.",
+                   need, kNoAllocScratchBytes);
+        return TECOOPS_STATUS_NOT_SUPPORTED;
+    }
+    if (p.max_splits > 1) {
+        int device = -1;
+        if (cudaGetDevice(&device) != cudaSuccess) return TECOOPS_STATUS_INTERNAL_ERROR;
+        void *scratch = scratchFor(device);   // the current device's copy of the array
+        if (scratch == nullptr) return TECOOPS_STATUS_INTERNAL_ERROR;
+        const size_t recs = (size_t)batch * heads * p.max_splits;
+        p.part_o = static_cast<float *>(scratch);
+        p.part_lse = p.part_o + recs * head_dim;
+    }
+    const cudaError_t e =
+        tecoops::kern::launch_decode(p, k->dataType == TECOOPS_DATA_BFLOAT16, handle->stream);
+    if (e != cudaSuccess) {
+        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: launch failed: %s", cudaGetErrorString(e));
+        return TECOOPS_STATUS_INTERNAL_ERROR;
+    }
+    return TECOOPS_STATUS_SUCCESS;
+}

@@ -28,7 +28,7 @@ EXPORTED = [
     "tecoopsGetTensor4dDescriptor", "tecoopsSetTensorNdDescriptor",
     "tecoopsGetTensorNdDescriptor", "tecoopsDestroyTensorDescriptor", "tecoopsMemset",
     "tecoopsReshapeAndCache", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
-    "tecoopsGetDeviceErrorStatus", "tecoopsFlattenRays", "tecoopsReduceVariance",
+    "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlattenRays", "tecoopsReduceVariance",
     "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsCausalConv1d",
 ]
 
@@ -70,6 +70,8 @@ def lib():
         "tecoopsGetFlashAttentionWorkspaceSize": [_vp, _i, _i, _vp, _vp, _vp,
                                                   ctypes.POINTER(ctypes.c_size_t)],
         "tecoopsGetDeviceErrorStatus": [_vp, ctypes.POINTER(_i)],
+        "tecoopsFlashAttentionDecodeNoAlloc": [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                               _vp, _vp, _vp, _vp],
         "tecoopsRmsNorm": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float],
     }
     for name, args in sig.items():
@@ -148,6 +150,16 @@ def flash_attention(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num, q
                                        _vp(block_table), q_desc.d, _vp(q), k_desc.d,
                                        _vp(k_cache), v_desc.d, _vp(v_cache), o_desc.d, _vp(out),
                                        _vp(workspace) if workspace else None)
+
+
+def flash_attention_decode_noalloc(handle: Handle, max_seqlen_k, q_seq_lens, kv_seq_lens,
+                                   bt_desc: Desc, block_table, q_desc: Desc, q, k_desc: Desc,
+                                   k_cache, v_desc: Desc, v_cache, o_desc: Desc, out) -> int:
+    """Decode for callers that cannot allocate: scratch is the library's static array."""
+    return lib().tecoopsFlashAttentionDecodeNoAlloc(handle.h, max_seqlen_k, _vp(q_seq_lens),
+                                                    _vp(kv_seq_lens), bt_desc.d, _vp(block_table),
+                                                    q_desc.d, _vp(q), k_desc.d, _vp(k_cache),
+                                                    v_desc.d, _vp(v_cache), o_desc.d, _vp(out))
 
 
 def workspace_size(handle: Handle, max_seqlen_q, max_seqlen_k, bt_desc: Desc, q_desc: Desc,

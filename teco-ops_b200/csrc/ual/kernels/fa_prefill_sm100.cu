@@ -8,21 +8,25 @@
 //   with K/V read from the paged cache [pages, Hkv, block_size, D] through
 //   block_table[b][j / block_size], kv head h / (Hq / Hkv).
 //
-// B200 design (one CTA = one 128-row Q tile of one q head):
-//   warp 0      TMA producer: Q tile once, then K/V tiles of 128 tokens assembled
-//               from 128/block_size page boxes of the 4-D cache tensor map (the page
-//               id is a TMA coordinate, so the gather costs nothing extra); 2-stage
-//               ring; pages past kv_len use an out-of-range page coordinate so TMA
-//               zero-fills them.  128-byte swizzle, 64-column boxes.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
-//                 S_j = Q K_j^T   (SS form, M=128, N=128, K=D, fp32 in TMEM, 2 buffers)
-//                 O  += P_j V_j   (TS form: P bf16/fp16 from TMEM, V MN-major in smem)
-//   warps 4-7   softmax: thread r owns row r = TMEM lane r; loads S with
-//               tcgen05.ld, masks (bottom-right causal + kv_len tail), online softmax in
-//               the exp2 domain with a lazy O rescale (only when the running max grows
-//               by more than 2^8), writes P back to TMEM with tcgen05.st, and runs the
-//               epilogue O / l -> global.
-// TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+D).
+// B200 design.  One CTA owns two 128-row Q sub-tiles that read the same KV head:
+// two heads of one GQA group over the same rows (group even), or two consecutive
+// row tiles of one head (group odd).  K/V tiles are loaded once for both.
+//   warp 0      TMA producer: both Q sub-tiles, then K/V tiles of 128 tokens assembled
+//               from 128/block_size page boxes of the 4-D cache tensor map (the page id
+//               is a TMA coordinate; pages past kv_len use an out-of-range coordinate
+//               so TMA zero-fills them); 2-stage ring; 128-byte swizzle, 64-column
+//               boxes.  It also clears V rows past kv_len in the last tile.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, ping-ponging the
+//               sub-tiles so the tensor core works on one while the other's softmax
+//               runs:  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), ...
+//                 S_X = Q_X K_j^T (SS form, M=128, N=128, K=D, fp32 in TMEM)
+//                 O_X += P_X V_j  (TS form: P read from TMEM, V MN-major in smem)
+//   warps 2-5   softmax of sub-tile 0, warps 6-9 of sub-tile 1: thread r owns
+//               row r = TMEM lane r (r = 32*(warp%4) + lane); two passes over the S row (max, then
+//               exp2/sum/pack with the 16-bit P written over the S columns it came
+//               from), tree reductions, lazy O rescale (only when the running max
+//               grows by more than 2^8), epilogue O / l -> global.
+// TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,256+D) O_1 [384,384+D).
 // Every mbarrier wait is bounded (~2 s); a wait that gives up records its site in
 // the device error word and the CTA drains its MMAs, frees TMEM and exits.
 #include <cuda.h>
@@ -44,24 +48,24 @@ using namespace sm100;
 
 namespace {
 
-constexpr int kBM = 128;        // Q rows per tile
+constexpr int kBM = 128;        // Q rows per sub-tile
 constexpr int kBN = 128;        // KV tokens per tile
-constexpr int kThreads = 256;
+constexpr int kThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-5 / 6-9 softmax of sub-tile 0 / 1
 constexpr uint32_t kTmemCols = 512;
+// TMEM columns: S_X at 128*X (P_X aliased on its first 64 columns), O_X at 256 + 128*X
 constexpr uint32_t kColS = 0;
-constexpr uint32_t kColP = 256;
-constexpr uint32_t kColO = 384;
+constexpr uint32_t kColO = 256;
 
 template <int D>
 struct PrefillSmem {
     static constexpr int kHalves = D / 64;
     static constexpr int kHalfBytes = 128 * 128;              // 128 rows x 128 B
-    static constexpr int kTileBytes = kHalves * kHalfBytes;   // Q, K or V tile
-    static constexpr int kQ = 0;
-    static constexpr int kK0 = kTileBytes;
-    static constexpr int kV0 = kK0 + 2 * kTileBytes;
+    static constexpr int kTileBytes = kHalves * kHalfBytes;   // one Q sub-tile, K or V tile
+    static constexpr int kQ0 = 0;                              // Q sub-tiles 0 and 1
+    static constexpr int kK0 = 2 * kTileBytes;                 // K stages 0, 1
+    static constexpr int kV0 = kK0 + 2 * kTileBytes;           // V stages 0, 1
     static constexpr int kBytes = kV0 + 2 * kTileBytes;
-    static constexpr int kAlloc = kBytes + 1024;   // slack for 1024-byte alignment
+    static constexpr int kAlloc = kBytes + 1024;               // 1024-byte alignment slack
 };
 
 struct PrefillParams {
@@ -73,11 +77,13 @@ struct PrefillParams {
     int num_heads;
     int num_kv_heads;
     int group;
+    int pair_heads;     // 1: sub-tiles are heads 2i, 2i+1 of one GQA group (same rows)
+                        // 0: sub-tiles are row tiles 2i, 2i+1 of one head
     int block_size;
     int rows_per_box;   // min(block_size, 128)
     int block_table_dim;
     int num_pages;
-    int num_qtiles;     // ceil(max_q / 128)
+    int num_units;      // grid.z: q-tiles (pair_heads) or q-tile pairs
     int total_q;
     float scale_log2;
 };
@@ -87,6 +93,22 @@ enum WaitSite : int {
     kSiteP = 0x600, kSiteO = 0x700, kSiteDrain = 0x800, kSiteVz = 0x900
 };
 
+// barrier slots
+constexpr int Q_FULL = 0, K_FULL = 1, V_FULL = 3, KV_EMPTY = 5, S_FULL = 7, P_FULL = 9,
+              O_DONE = 11, V_ZERO = 13, DRAIN = 14, NUM_BARS = 15;
+
+__device__ __forceinline__ float max4tree(const uint32_t (&u)[32], int base, int klim, bool mask,
+                                          float acc) {
+    float m[4] = {acc, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        float x = __uint_as_float(u[e]);
+        if (mask && base + e > klim) x = -INFINITY;
+        m[e & 3] = fmaxf(m[e & 3], x);
+    }
+    return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
 }  // namespace
 
 template <typename T, int D>
@@ -95,64 +117,62 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap, PrefillParams p) {
     using Sm = PrefillSmem<D>;
-    constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+    constexpr bool kBF16 = !std::is_same<T, __half>::value;
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[16];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
 
-    const int h = blockIdx.x;
     const int b = blockIdx.y;
-    const int qt = p.num_qtiles - 1 - (int)blockIdx.z;   // heaviest tiles launch first
+    const int unit = p.num_units - 1 - (int)blockIdx.z;   // heaviest units launch first
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     const int L = __ldg(p.q_seq_lens + b);
     const int S = __ldg(p.kv_seq_lens + b);
-    const int q0 = qt * kBM;
-    if (q0 >= L) return;   // uniform: tile beyond this sequence
-    const int rows_valid = min(kBM, L - q0);
-    const int off = S - L;                                   // bottom-right causal offset
-    const int kv_hi = min(S, off + q0 + rows_valid);         // exclusive key bound of tile
-    const int n_tiles = kv_hi > 0 ? (kv_hi + kBN - 1) / kBN : 0;
-    const int kvh = h / p.group;
+    const int off = S - L;   // bottom-right causal offset: row i attends keys <= off + i
+    // the two sub-tiles of this CTA
+    int hX[2], q0X[2], rowsX[2], nX[2];
+#pragma unroll
+    for (int X = 0; X < 2; ++X) {
+        if (p.pair_heads) {
+            hX[X] = 2 * (int)blockIdx.x + X;
+            q0X[X] = unit * kBM;
+        } else {
+            hX[X] = (int)blockIdx.x;
+            q0X[X] = unit * 2 * kBM + X * kBM;
+        }
+        rowsX[X] = min(kBM, L - q0X[X]);
+        const int kv_hi = rowsX[X] > 0 ? min(S, off + q0X[X] + rowsX[X]) : 0;
+        nX[X] = (rowsX[X] > 0 && kv_hi > 0) ? (kv_hi + kBN - 1) / kBN : 0;
+    }
+    if (rowsX[0] <= 0 && rowsX[1] <= 0) return;   // uniform: unit beyond this sequence
+    const int N = max(nX[0], nX[1]);
+    const int kvh = hX[0] / p.group;
 
-    // 1024-byte aligned dynamic smem base
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t sbase = (raw_base + 1023u) & ~1023u;
     uint8_t *sgen = smem_raw + (sbase - raw_base);
-
     const uint32_t bar0 = smem_u32(&bars[0]);
     auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
-    // barrier ids
-    constexpr int Q_FULL = 0, K_FULL = 1, V_FULL = 3, KV_EMPTY = 5, S_FULL = 7, P_FULL = 9,
-                  O_DONE = 11, DRAIN = 12;
 
-    if (n_tiles == 0) {
-        // no admissible key for any row (q_len > kv_len): write zeros
-        if (warp >= 4) {
-            const int r = threadIdx.x - 128;
-            const int qs = warp_seq_start(p.q_seq_lens, b);
-            if (r < rows_valid && qs + q0 + r < p.total_q) {
-                T *o = static_cast<T *>(p.out) + ((int64_t)(qs + q0 + r) * p.num_heads + h) * D;
-                for (int d = 0; d < D; ++d) o[d] = Elem<T>::from_float(0.f);
-            }
+    // rows of a sub-tile that have no admissible key (q_len > kv_len) are written as zeros
+    if (warp >= 2) {
+        const int X = (warp - 2) >> 2;
+        const int r = 32 * (warp & 3) + lane;
+        const int qs = warp_seq_start(p.q_seq_lens, b);
+        const int nx = X ? nX[1] : nX[0], rx = X ? rowsX[1] : rowsX[0];
+        const int qx = X ? q0X[1] : q0X[0], hx = X ? hX[1] : hX[0];
+        if (nx == 0 && r < rx && qs + qx + r < p.total_q) {
+            T *o = static_cast<T *>(p.out) + ((int64_t)(qs + qx + r) * p.num_heads + hx) * D;
+            for (int d = 0; d < D; ++d) o[d] = Elem<T>::from_float(0.f);
         }
-        return;
     }
+    if (N == 0) return;   // uniform
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        mbar_init(BAR(Q_FULL), 1);
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(BAR(K_FULL + s), 1);
-            mbar_init(BAR(V_FULL + s), 1);
-            mbar_init(BAR(KV_EMPTY + s), 1);
-            mbar_init(BAR(S_FULL + s), 1);
-            mbar_init(BAR(P_FULL + s), 128);
-        }
-        mbar_init(BAR(O_DONE), 1);
-        mbar_init(BAR(DRAIN), 1);
+        for (int i = 0; i < NUM_BARS; ++i) mbar_init(BAR(i), (i == P_FULL || i == P_FULL + 1) ? 128 : 1);
         mbar_fence_init();
     }
     if (warp == 1) {
@@ -164,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     volatile int *abortp = &abort_flag;
+    const bool last_partial = N * kBN > S;   // last KV tile holds rows past kv_len
 
     if (warp == 0) {
         // ===================== TMA producer =====================
@@ -172,17 +193,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&qmap);
             tma_prefetch_desc(&kmap);
             tma_prefetch_desc(&vmap);
-            mbar_arrive_expect_tx(BAR(Q_FULL), Sm::kTileBytes);
+            uint32_t qbytes = 0;
 #pragma unroll
-            for (int hh = 0; hh < Sm::kHalves; ++hh)
-                tma_load_3d(sbase + Sm::kQ + hh * Sm::kHalfBytes, &qmap, BAR(Q_FULL), hh * 64, h,
-                            qs + q0);
+            for (int X = 0; X < 2; ++X)
+                if (nX[X] > 0) qbytes += Sm::kTileBytes;
+            mbar_arrive_expect_tx(BAR(Q_FULL), qbytes);
+#pragma unroll
+            for (int X = 0; X < 2; ++X) {
+                if (nX[X] == 0) continue;
+#pragma unroll
+                for (int hh = 0; hh < Sm::kHalves; ++hh)
+                    tma_load_3d(sbase + Sm::kQ0 + X * Sm::kTileBytes + hh * Sm::kHalfBytes, &qmap,
+                                BAR(Q_FULL), hh * 64, hX[X], qs + q0X[X]);
+            }
         }
         const int rpb = p.rows_per_box;
         const int nbox = kBN / rpb;
         const int *bt = p.block_table + (int64_t)b * p.block_table_dim;
         int issued[2] = {0, 0};
-        for (int j = 0; j < n_tiles; ++j) {
+        for (int j = 0; j < N; ++j) {
             const int s = j & 1;
             if (j >= 2 && !mbar_wait_bounded(BAR(KV_EMPTY + s), ((j >> 1) - 1) & 1, abortp,
                                              p.dev_error, kSiteEmpty + j))
@@ -213,6 +242,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             issued[s] = j + 1;
         }
+        // rows of the last V tile past kv_len may hold arbitrary bits (unwritten cache
+        // slots): zero them before the PV MMAs of that tile read them
+        if (last_partial && issued[(N - 1) & 1] == N) {
+            const int s = (N - 1) & 1;
+            if (mbar_wait_bounded(BAR(V_FULL + s), ((N - 1) >> 1) & 1, abortp, p.dev_error,
+                                  kSiteVz)) {
+                const int first = S - (N - 1) * kBN;   // first row to clear
+                uint8_t *vt = sgen + Sm::kV0 + s * Sm::kTileBytes;
+                for (int r = first + lane; r < kBN; r += 32) {
+#pragma unroll
+                    for (int hh = 0; hh < Sm::kHalves; ++hh) {
+                        uint4 *q4 = reinterpret_cast<uint4 *>(vt + hh * Sm::kHalfBytes + r * 128);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) q4[e] = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(BAR(V_ZERO));
+            }
+        }
         // on abort: let this warp's own copies in flight land before the CTA exits
         if (*abortp && lane == 0) {
             for (int s = 0; s < 2; ++s) {
@@ -229,95 +279,116 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc_pv = idesc_f16(kBF16, true, kBM, D);
             bool ok = mbar_wait_bounded(BAR(Q_FULL), 0, abortp, p.dev_error, kSiteQ);
             tc_fence_after();
-            auto issue_pv = [&](int i) -> bool {
-                const int s = i & 1;
-                if (!mbar_wait_bounded(BAR(P_FULL + s), (i >> 1) & 1, abortp, p.dev_error,
-                                       kSiteP + i))
-                    return false;
-                if (!mbar_wait_bounded(BAR(V_FULL + s), (i >> 1) & 1, abortp, p.dev_error,
-                                       kSiteV + i))
-                    return false;
-                tc_fence_after();
-                const uint32_t vbase = sbase + Sm::kV0 + s * Sm::kTileBytes;
-#pragma unroll
-                for (int t = 0; t < kBN / 16; ++t) {
-                    const uint64_t bdesc =
-                        smem_desc_sw128(vbase + t * 16 * 128, Sm::kHalfBytes, 1024);
-                    tc_mma_ts(tmem + kColO, tmem + kColP + s * 64 + t * 8, bdesc, idesc_pv,
-                              (i > 0 || t > 0) ? 1u : 0u);
-                }
-                tc_commit(BAR(O_DONE));
-                tc_commit(BAR(KV_EMPTY + s));
-                return true;
-            };
-            for (int j = 0; ok && j < n_tiles; ++j) {
-                const int s = j & 1;
-                if (!mbar_wait_bounded(BAR(K_FULL + s), (j >> 1) & 1, abortp, p.dev_error,
-                                       kSiteK + j)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t kbase = sbase + Sm::kK0 + s * Sm::kTileBytes;
+            auto issue_s = [&](int X, int j) {
+                const uint32_t kbase = sbase + Sm::kK0 + (j & 1) * Sm::kTileBytes;
+                const uint32_t qbase = sbase + Sm::kQ0 + X * Sm::kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t koff = (kk >> 2) * Sm::kHalfBytes + (kk & 3) * 32;
-                    const uint64_t adesc = smem_desc_sw128(sbase + Sm::kQ + koff, 16, 1024);
-                    const uint64_t bdesc = smem_desc_sw128(kbase + koff, 16, 1024);
-                    tc_mma_ss(tmem + kColS + s * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+                    tc_mma_ss(tmem + kColS + X * 128, smem_desc_sw128(qbase + koff, 16, 1024),
+                              smem_desc_sw128(kbase + koff, 16, 1024), idesc_qk,
+                              kk > 0 ? 1u : 0u);
                 }
-                tc_commit(BAR(S_FULL + s));
-                if (j >= 1 && !issue_pv(j - 1)) {
+                tc_commit(BAR(S_FULL + X));
+            };
+            auto wait_k = [&](int j) {
+                if (!mbar_wait_bounded(BAR(K_FULL + (j & 1)), (j >> 1) & 1, abortp, p.dev_error,
+                                       kSiteK + j))
+                    return false;
+                tc_fence_after();
+                return true;
+            };
+            if (ok) ok = wait_k(0);
+            if (ok) {
+                if (nX[0] > 0) issue_s(0, 0);
+                if (nX[1] > 0) issue_s(1, 0);
+            }
+            for (int j = 0; ok && j < N; ++j) {
+                const int s = j & 1;
+                if (!mbar_wait_bounded(BAR(V_FULL + s), (j >> 1) & 1, abortp, p.dev_error,
+                                       kSiteV + j)) {
                     ok = false;
                     break;
                 }
+                if (j == N - 1 && last_partial &&
+                    !mbar_wait_bounded(BAR(V_ZERO), 0, abortp, p.dev_error, kSiteVz)) {
+                    ok = false;
+                    break;
+                }
+                bool next_k_ready = false;
+#pragma unroll
+                for (int X = 0; X < 2; ++X) {
+                    if (j >= nX[X]) continue;
+                    if (!mbar_wait_bounded(BAR(P_FULL + X), j & 1, abortp, p.dev_error,
+                                           kSiteP + j)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t vbase = sbase + Sm::kV0 + s * Sm::kTileBytes;
+#pragma unroll
+                    for (int t = 0; t < kBN / 16; ++t)
+                        tc_mma_ts(tmem + kColO + X * 128, tmem + kColS + X * 128 + t * 8,
+                                  smem_desc_sw128(vbase + t * 16 * 128, Sm::kHalfBytes, 1024),
+                                  idesc_pv, (j > 0 || t > 0) ? 1u : 0u);
+                    if (j + 1 < nX[X]) {
+                        if (!next_k_ready) {
+                            if (!wait_k(j + 1)) {
+                                ok = false;
+                                break;
+                            }
+                            next_k_ready = true;
+                        }
+                        issue_s(X, j + 1);
+                    } else {
+                        tc_commit(BAR(O_DONE + X));
+                    }
+                }
+                if (!ok) break;
+                tc_commit(BAR(KV_EMPTY + s));
             }
-            if (ok) issue_pv(n_tiles - 1);
             // drain: every MMA issued by this thread has completed before TMEM is freed
             tc_commit(BAR(DRAIN));
             mbar_wait_bounded(BAR(DRAIN), 0, nullptr, p.dev_error, kSiteDrain);
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    } else {
         // ===================== softmax + epilogue (one row per thread) =====================
-        const int r = threadIdx.x - 128;
+        // warps 2-5 serve sub-tile 0 and warps 6-9 sub-tile 1; a warp may only touch
+        // TMEM lanes 32*(warp%4) .. +31, so row r = 32*(warp%4) + lane
+        const int X = (warp - 2) >> 2;
+        const int r = 32 * (warp & 3) + lane;
+        const int n = X ? nX[1] : nX[0];
+        const int rows = X ? rowsX[1] : rowsX[0];
+        const int hx = X ? hX[1] : hX[0];
         const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
-        const int qi = q0 + r;
-        const int lim = off + qi;   // last admissible key of this row (inclusive)
+        const uint32_t tS = tmem + lane_addr + kColS + X * 128;
+        const uint32_t tO = tmem + lane_addr + kColO + X * 128;
+        const int qi = (X ? q0X[1] : q0X[0]) + r;
+        const int klim = min(off + qi, S - 1);   // last admissible key of this row
         const float sl2 = p.scale_log2;
         const int qs = warp_seq_start(p.q_seq_lens, b);
-        float m_s = -INFINITY;       // running max in scaled (log2) units
+        float m_s = -INFINITY;   // running max, scaled (log2) units
         float l = 0.f;
         bool ok = true;
-        for (int j = 0; j < n_tiles && ok; ++j) {
-            const int s = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(S_FULL + s), (j >> 1) & 1, abortp, p.dev_error,
-                                   kSiteS + j))) {
+        for (int j = 0; j < n; ++j) {
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(S_FULL + X), j & 1, abortp,
+                                                           p.dev_error, kSiteS + j))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float x[kBN];
-            {
-                uint32_t u[32];
-#pragma unroll
-                for (int c = 0; c < kBN / 32; ++c) {
-                    tmem_ld32(tmem + lane_addr + kColS + s * 128 + c * 32, u);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]);
-                }
-            }
             const int kbase = j * kBN;
-            const int klim = min(lim, S - 1);   // inclusive admissible bound
-            if (kbase + kBN - 1 > klim) {
-#pragma unroll
-                for (int c = 0; c < kBN; ++c)
-                    if (kbase + c > klim) x[c] = -INFINITY;
-            }
+            const bool mask = kbase + kBN - 1 > klim;
+            // pass 1: row max over the 128 scores
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, x[c]);
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t u[32];
+                tmem_ld32(tS + c * 32, u);
+                tmem_ld_wait();
+                mx = max4tree(u, kbase + c * 32, klim, mask, mx);
+            }
             const float m_new = fmaxf(m_s, mx * sl2);
             const bool need = (j == 0) || (m_new > m_s + 8.0f);
             const bool warp_need = __any_sync(0xffffffffu, need);
@@ -327,82 +398,60 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_s = m_new;
             }
             const float m_use = (m_s == -INFINITY) ? 0.f : m_s;
-            float rs = 0.f;
-            uint32_t pk[kBN / 2];
-#pragma unroll
-            for (int c = 0; c < kBN; c += 2) {
-                const float p0 = fast_exp2(fmaf(x[c], sl2, -m_use));
-                const float p1 = fast_exp2(fmaf(x[c + 1], sl2, -m_use));
-                rs += p0 + p1;
-                pk[c / 2] = Elem<T>::pack2(p0, p1);
-            }
-            l = l * alpha + rs;
-
-            if (j >= 1) {
-                // PV_{j-1} complete: O is stable and P buffer s is free
-                if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(O_DONE), (j - 1) & 1, abortp, p.dev_error,
-                                       kSiteO + j))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                if (warp_need) {
-#pragma unroll
-                    for (int c = 0; c < D / 32; ++c) {
-                        uint32_t u[32];
-                        const uint32_t a = tmem + lane_addr + kColO + c * 32;
-                        tmem_ld32(a, u);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-                        tmem_st32(a, u);
-                    }
-                }
-            }
-            if (j == n_tiles - 1 && kbase + kBN > S) {
-                // rows of the last V tile past kv_len may hold arbitrary bits: zero them
-                if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(V_FULL + s), (j >> 1) & 1, abortp, p.dev_error,
-                                       kSiteVz))) {
-                    ok = false;
-                    break;
-                }
-                if (kbase + r >= S) {
-                    uint8_t *vrow = sgen + Sm::kV0 + s * Sm::kTileBytes + r * 128;
-#pragma unroll
-                    for (int hh = 0; hh < Sm::kHalves; ++hh) {
-                        uint4 *q4 = reinterpret_cast<uint4 *>(vrow + hh * Sm::kHalfBytes);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) q4[e] = make_uint4(0, 0, 0, 0);
-                    }
-                }
-                fence_proxy_async_smem();
-            }
-            {
+            // pass 2: p = 2^(s*scale - m), row sum, P (16-bit) written over the S columns
+            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+            for (int c = 0; c < kBN / 32; ++c) {
                 uint32_t u[32];
+                tmem_ld32(tS + c * 32, u);
+                tmem_ld_wait();
+                uint32_t pk[16];
 #pragma unroll
-                for (int c = 0; c < kBN / 64; ++c) {
+                for (int e = 0; e < 32; e += 2) {
+                    float x0 = __uint_as_float(u[e]), x1 = __uint_as_float(u[e + 1]);
+                    if (mask) {
+                        if (kbase + c * 32 + e > klim) x0 = -INFINITY;
+                        if (kbase + c * 32 + e + 1 > klim) x1 = -INFINITY;
+                    }
+                    const float p0 = fast_exp2(fmaf(x0, sl2, -m_use));
+                    const float p1 = fast_exp2(fmaf(x1, sl2, -m_use));
+                    rs[(e >> 1) & 3] += p0 + p1;
+                    pk[e >> 1] = Elem<T>::pack2(p0, p1);
+                }
+                tmem_st16(tS + c * 16, pk);
+            }
+            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            // O rescale: PV_{j-1} has completed (S_j, issued after it, has)
+            if (j > 0 && warp_need) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) u[e] = pk[c * 32 + e];
-                    tmem_st32(tmem + lane_addr + kColP + s * 64 + c * 32, u);
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t u[32];
+                    tmem_ld32(tO + c * 32, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+                    tmem_st32(tO + c * 32, u);
                 }
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(BAR(P_FULL + s));
+            mbar_arrive(BAR(P_FULL + X));
         }
         // epilogue
-        if (__all_sync(0xffffffffu, ok && mbar_wait_bounded(BAR(O_DONE), (n_tiles - 1) & 1,
-                                                            abortp, p.dev_error, kSiteO + 0xff))) {
+        if (n > 0 &&
+            __all_sync(0xffffffffu, ok && mbar_wait_bounded(BAR(O_DONE + X), 0, abortp,
+                                                            p.dev_error, kSiteO + X))) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            T *orow = static_cast<T *>(p.out) + ((int64_t)(qs + qi) * p.num_heads + h) * D;
+            const bool store = r < rows && qs + qi < p.total_q;
+            T *orow = static_cast<T *>(p.out) + ((int64_t)(qs + qi) * p.num_heads + hx) * D;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
                 uint32_t u[32];
-                tmem_ld32(tmem + lane_addr + kColO + c * 32, u);
+                tmem_ld32(tO + c * 32, u);
                 tmem_ld_wait();
-                if (r < rows_valid && qs + qi < p.total_q) {
+                if (store) {
                     uint32_t pkd[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
@@ -506,20 +555,22 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, cudaStre
     p.num_heads = s.num_heads;
     p.num_kv_heads = s.num_kv_heads;
     p.group = s.num_heads / s.num_kv_heads;
+    p.pair_heads = (p.group % 2 == 0) ? 1 : 0;
     p.block_size = s.block_size;
     p.rows_per_box = rpb;
     p.block_table_dim = s.block_table_dim;
     p.num_pages = s.num_pages;
-    p.num_qtiles = (s.max_q + kBM - 1) / kBM;
+    const int nqt = (s.max_q + kBM - 1) / kBM;
+    p.num_units = p.pair_heads ? nqt : (nqt + 1) / 2;
     p.total_q = s.total_q;
     p.scale_log2 = s.scale_log2;
-    if (p.num_qtiles <= 0 || s.batch <= 0) return cudaSuccess;
+    if (p.num_units <= 0 || s.batch <= 0) return cudaSuccess;
 
     auto kfn = fa_prefill_sm100_kernel<T, D>;
     const int smem = PrefillSmem<D>::kAlloc;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(s.num_heads, s.batch, p.num_qtiles);
+    dim3 grid(p.pair_heads ? s.num_heads / 2 : s.num_heads, s.batch, p.num_units);
     kfn<<<grid, kThreads, smem, stream>>>(qmap, kmap, vmap, p);
     return cudaGetLastError();
 }

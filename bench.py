@@ -92,58 +92,59 @@ def config2_lens(seed=10):
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
-
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled through NVML every 10 ms while the
+    timed regions run (reading only; no setting is changed)."""
 
     def __init__(self, device_index: int):
         self.dev = device_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.smax = None
+        self._stop = threading.Event()
+        self.t = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.dev]) if vis and vis.split(",")[0].isdigit() else self.dev
+            self.h = nv.nvmlDeviceGetHandleByIndex(idx)
+            self.nv = nv
+            self.smax = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except Exception:
-            self.proc = None
+        except Exception as e:  # NVML unavailable: report it
+            self.err = str(e)
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+            except Exception:
+                pass
+            time.sleep(0.01)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
+        if self.t is None:
+            return {"sm_mhz": None, "sm_max_mhz": None,
+                    "reasons": ["nvml unavailable: " + getattr(self, "err", "?")]}
+        self._stop.set()
+        self.t.join(timeout=2)
+        nv = self.nv
+        names = {nv.nvmlClocksEventReasonHwSlowdown: "hw_slowdown",
+                 nv.nvmlClocksEventReasonHwThermalSlowdown: "hw_thermal_slowdown",
+                 nv.nvmlClocksEventReasonSwThermalSlowdown: "sw_thermal_slowdown",
+                 nv.nvmlClocksEventReasonSwPowerCap: "sw_power_cap"}
+        reasons = set()
+        for _, r in self.samples:
+            for bit, n in names.items():
+                if r & bit:
                     reasons.add(n)
-        sm.sort()
-        med = sm[len(sm) // 2] if sm else None
-        return {"sm_mhz": med, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = sorted(c for c, _ in self.samples)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": self.smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -342,7 +343,6 @@ def run_ours(args):
     clocks.start()
     times = timed_loop(torch, args.steps, args.warmup, [W.reshape2, W.prefill2], flush=W.flush)
     barrier()
-    clk = clocks.stop()
     t_reshape, t_prefill = times
     step_ms = [a + b for a, b in zip(t_reshape, t_prefill)]
     total_ms = max_over_ranks(sum(step_ms))
@@ -377,6 +377,7 @@ def run_ours(args):
     barrier()
     (t4,) = timed_loop(torch, args.steps, args.warmup, [W.reshape4])
     r_ms = max_over_ranks(sum(t4))
+    clk = clocks.stop()   # sampled across every timed region above
     reshape = {
         "workload": "config 4: T=65536 scattered slots, 0% padding, 65536-page cache, bf16",
         "metric": "reshape_and_cache HBM GB/s", "unit": "GB/s",
@@ -550,7 +551,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")

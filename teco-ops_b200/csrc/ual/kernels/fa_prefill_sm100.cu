@@ -97,16 +97,41 @@ enum WaitSite : int {
 constexpr int Q_FULL = 0, K_FULL = 1, V_FULL = 3, KV_EMPTY = 5, S_FULL = 7, P_FULL = 9,
               O_DONE = 11, V_ZERO = 13, DRAIN = 14, NUM_BARS = 15;
 
-__device__ __forceinline__ float max4tree(const uint32_t (&u)[32], int base, int klim, bool mask,
-                                          float acc) {
+// max of 32 scores (u) and acc; columns at or past `nv` are excluded when MASKED
+template <bool MASKED>
+__device__ __forceinline__ float chunk_max(const uint32_t (&u)[32], int nv, float acc) {
     float m[4] = {acc, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        float x = __uint_as_float(u[e]);
-        if (mask && base + e > klim) x = -INFINITY;
-        m[e & 3] = fmaxf(m[e & 3], x);
+    for (int e = 0; e < 32; e += 2) {
+        float x0 = __uint_as_float(u[e]), x1 = __uint_as_float(u[e + 1]);
+        if (MASKED) {
+            x0 = e < nv ? x0 : -INFINITY;
+            x1 = e + 1 < nv ? x1 : -INFINITY;
+        }
+        m[(e >> 1) & 3] = fmax3(m[(e >> 1) & 3], x0, x1);
     }
-    return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+    return fmax3(m[0], fmax3(m[1], m[2], m[3]), -INFINITY);
+}
+
+// p = 2^(s*scale - m) for 32 scores, packed to 16-bit pairs; row sum accumulated
+// in two packed fp32 accumulators
+template <typename T, bool MASKED>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&u)[32], int nv, uint64_t sl2x2,
+                                          uint64_t negm2, uint64_t (&sum)[2],
+                                          uint32_t (&pk)[16]) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+        float x0 = __uint_as_float(u[e]), x1 = __uint_as_float(u[e + 1]);
+        if (MASKED) {
+            x0 = e < nv ? x0 : -INFINITY;
+            x1 = e + 1 < nv ? x1 : -INFINITY;
+        }
+        float t0, t1;
+        f2unpack(ffma2(f2pack(x0, x1), sl2x2, negm2), t0, t1);
+        const float p0 = fast_exp2(t0), p1 = fast_exp2(t1);
+        sum[(e >> 1) & 1] = fadd2(sum[(e >> 1) & 1], f2pack(p0, p1));
+        pk[e >> 1] = Elem<T>::pack2(p0, p1);
+    }
 }
 
 }  // namespace
@@ -379,15 +404,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const int kbase = j * kBN;
-            const bool mask = kbase + kBN - 1 > klim;
-            // pass 1: row max over the 128 scores
+            // columns kbase + c >= kbase + nvalid are masked (causal / kv_len tail)
+            const int nvalid = klim - kbase + 1;
+            const bool masked = __any_sync(0xffffffffu, nvalid < kBN);
+            // pass 1: row max over the 128 scores, two TMEM loads in flight per wait
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t u[32];
-                tmem_ld32(tS + c * 32, u);
+            for (int c = 0; c < kBN / 32; c += 2) {
+                uint32_t u0[32], u1[32];
+                tmem_ld32(tS + c * 32, u0);
+                tmem_ld32(tS + c * 32 + 32, u1);
                 tmem_ld_wait();
-                mx = max4tree(u, kbase + c * 32, klim, mask, mx);
+                if (masked) {
+                    mx = chunk_max<true>(u0, nvalid - c * 32, mx);
+                    mx = chunk_max<true>(u1, nvalid - c * 32 - 32, mx);
+                } else {
+                    mx = chunk_max<false>(u0, 32, mx);
+                    mx = chunk_max<false>(u1, 32, mx);
+                }
             }
             const float m_new = fmaxf(m_s, mx * sl2);
             const bool need = (j == 0) || (m_new > m_s + 8.0f);
@@ -399,28 +433,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float m_use = (m_s == -INFINITY) ? 0.f : m_s;
             // pass 2: p = 2^(s*scale - m), row sum, P (16-bit) written over the S columns
-            float rs[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
+            const uint64_t sl2x2 = f2pack(sl2, sl2);
+            const uint64_t negm2 = f2pack(-m_use, -m_use);
+            uint64_t sum2[2] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
+#pragma unroll
             for (int c = 0; c < kBN / 32; ++c) {
                 uint32_t u[32];
                 tmem_ld32(tS + c * 32, u);
                 tmem_ld_wait();
                 uint32_t pk[16];
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float x0 = __uint_as_float(u[e]), x1 = __uint_as_float(u[e + 1]);
-                    if (mask) {
-                        if (kbase + c * 32 + e > klim) x0 = -INFINITY;
-                        if (kbase + c * 32 + e + 1 > klim) x1 = -INFINITY;
-                    }
-                    const float p0 = fast_exp2(fmaf(x0, sl2, -m_use));
-                    const float p1 = fast_exp2(fmaf(x1, sl2, -m_use));
-                    rs[(e >> 1) & 3] += p0 + p1;
-                    pk[e >> 1] = Elem<T>::pack2(p0, p1);
-                }
+                if (masked)
+                    chunk_exp<T, true>(u, nvalid - c * 32, sl2x2, negm2, sum2, pk);
+                else
+                    chunk_exp<T, false>(u, 32, sl2x2, negm2, sum2, pk);
                 tmem_st16(tS + c * 16, pk);
             }
-            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            float s0, s1, s2, s3;
+            f2unpack(sum2[0], s0, s1);
+            f2unpack(sum2[1], s2, s3);
+            l = l * alpha + ((s0 + s1) + (s2 + s3));
             // O rescale: PV_{j-1} has completed (S_j, issued after it, has)
             if (j > 0 && warp_need) {
 #pragma unroll

@@ -11,20 +11,26 @@
 // B200 design.  One CTA owns two 128-row Q sub-tiles that read the same KV head:
 // two heads of one GQA group over the same rows (group even), or two consecutive
 // row tiles of one head (group odd).  K/V tiles are loaded once for both.
-//   warp 0      TMA producer: both Q sub-tiles, then K/V tiles of 128 tokens assembled
+//   warps 0, 10 TMA producers (warp 0: both Q sub-tiles and the K ring; warp 10: the
+//               V ring), K/V tiles of 128 tokens assembled
 //               from 128/block_size page boxes of the 4-D cache tensor map (the page id
 //               is a TMA coordinate; pages past kv_len use an out-of-range coordinate
-//               so TMA zero-fills them); 2-stage ring; 128-byte swizzle, 64-column
-//               boxes.  It also clears V rows past kv_len in the last tile.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, ping-ponging the
-//               sub-tiles so the tensor core works on one while the other's softmax
-//               runs:  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), ...
+//               so TMA zero-fills them); K ring of 3 stages released as soon as the S
+//               MMAs reading a tile are done, V ring of 2 stages released after the
+//               PV MMAs; 128-byte swizzle, 64-column boxes.  Warp 10 also clears V rows past
+//               kv_len in the last tile.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, fixed order
+//               PV_0(j) S_0(j+1) | PV_1(j) S_1(j+1) | ... with every operand of a pair
+//               awaited before its 16 MMAs go out back-to-back (the issue queue is
+//               shallow, so gaps between groups idle the tensor pipe):
 //                 S_X = Q_X K_j^T (SS form, M=128, N=128, K=D, fp32 in TMEM)
 //                 O_X += P_X V_j  (TS form: P read from TMEM, V MN-major in smem)
 //   warps 2-5   softmax of sub-tile 0, warps 6-9 of sub-tile 1: thread r owns
-//               row r = TMEM lane r (r = 32*(warp%4) + lane); two passes over the S row (max, then
-//               exp2/sum/pack with the 16-bit P written over the S columns it came
-//               from), tree reductions, lazy O rescale (only when the running max
+//               row r = TMEM lane r (r = 32*(warp%4) + lane); the 128-score row is
+//               read from TMEM in one burst, max by 3-input max trees, exp2 on the
+//               MUFU unit for 10 of every 16 pairs and by a fitted polynomial on the
+//               FMA pipe for the rest (packed f32x2 arithmetic), 16-bit P written over
+//               the S columns it came from, lazy O rescale (only when the running max
 //               grows by more than 2^8), epilogue O / l -> global.
 // TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,256+D) O_1 [384,384+D).
 // Every mbarrier wait is bounded (~2 s); a wait that gives up records its site in
@@ -50,7 +56,8 @@ namespace {
 
 constexpr int kBM = 128;        // Q rows per sub-tile
 constexpr int kBN = 128;        // KV tokens per tile
-constexpr int kThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-5 / 6-9 softmax of sub-tile 0 / 1
+constexpr int kThreads = 352;   // warp 0 Q/K producer, warp 1 MMA, warps 2-5 / 6-9 softmax
+                                // of sub-tile 0 / 1, warp 10 V producer
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: S_X at 128*X (P_X aliased on its first 64 columns), O_X at 256 + 128*X
 constexpr uint32_t kColS = 0;
@@ -62,8 +69,8 @@ struct PrefillSmem {
     static constexpr int kHalfBytes = 128 * 128;              // 128 rows x 128 B
     static constexpr int kTileBytes = kHalves * kHalfBytes;   // one Q sub-tile, K or V tile
     static constexpr int kQ0 = 0;                              // Q sub-tiles 0 and 1
-    static constexpr int kK0 = 2 * kTileBytes;                 // K stages 0, 1
-    static constexpr int kV0 = kK0 + 2 * kTileBytes;           // V stages 0, 1
+    static constexpr int kK0 = 2 * kTileBytes;                 // K stages 0..2
+    static constexpr int kV0 = kK0 + 3 * kTileBytes;           // V stages 0, 1
     static constexpr int kBytes = kV0 + 2 * kTileBytes;
     static constexpr int kAlloc = kBytes + 1024;               // 1024-byte alignment slack
 };
@@ -88,14 +95,30 @@ struct PrefillParams {
     float scale_log2;
 };
 
+#ifdef TECOOPS_PREFILL_TRACE
+// Development-only timeline capture (not built into the library): per CTA, clock64()
+// stamps of the pipeline events, read back with tecoops_prefill_trace_read.
+__device__ long long g_prefill_trace[8192 * 128];
+#define PTRACE(slot, v)                                                                  \
+    do {                                                                                 \
+        const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
+        if (cta_ < 8192) g_prefill_trace[cta_ * 128 + (slot)] = (long long)(v);          \
+    } while (0)
+#else
+#define PTRACE(slot, v) \
+    do {                \
+    } while (0)
+#endif
+
 enum WaitSite : int {
     kSiteQ = 0x100, kSiteK = 0x200, kSiteV = 0x300, kSiteEmpty = 0x400, kSiteS = 0x500,
     kSiteP = 0x600, kSiteO = 0x700, kSiteDrain = 0x800, kSiteVz = 0x900
 };
 
 // barrier slots
-constexpr int Q_FULL = 0, K_FULL = 1, V_FULL = 3, KV_EMPTY = 5, S_FULL = 7, P_FULL = 9,
-              O_DONE = 11, V_ZERO = 13, DRAIN = 14, NUM_BARS = 15;
+constexpr int kKStages = 3, kVStages = 2;
+constexpr int Q_FULL = 0, K_FULL = 1, K_EMPTY = 4, V_FULL = 7, V_EMPTY = 9, S_FULL = 11,
+              P_FULL = 13, O_DONE = 15, V_ZERO = 17, DRAIN = 18, NUM_BARS = 19;
 
 // max of 32 scores (u) and acc; columns at or past `nv` are excluded when MASKED
 template <bool MASKED>
@@ -113,6 +136,33 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&u)[32], int nv, floa
     return fmax3(m[0], fmax3(m[1], m[2], m[3]), -INFINITY);
 }
 
+// 2^x for a pair of finite x on the FMA/ALU pipes, to take load off the MUFU unit:
+// x = n + f with n = rint(x) (via the 1.5*2^23 rounding constant) and f in [-0.5, 0.5];
+// 2^f by a degree-3 polynomial 1 + f(c1 + f(c2 + f c3)) fitted here for minimum
+// relative error on [-0.5, 0.5] (max relative error 1.0e-4, far below the 2^-8
+// resolution of the 16-bit P it feeds); 2^n is added into the exponent field.
+// x is clamped at -125 (the result is then ~2e-38, i.e. zero for P; the exponent
+// field of p (126 or 127) minus 125 stays positive).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float &y1) {
+    constexpr float kRound = 12582912.f;   // 1.5 * 2^23
+    x0 = fmaxf(x0, -125.f);
+    x1 = fmaxf(x1, -125.f);
+    const uint64_t x2 = f2pack(x0, x1);
+    const uint64_t t2 = fadd2(x2, f2pack(kRound, kRound));          // round(x) in low bits
+    const uint64_t r2 = fadd2(t2, f2pack(-kRound, -kRound));        // round(x) as float
+    const uint64_t fr = ffma2(r2, f2pack(-1.f, -1.f), x2);          // f = x - round(x)
+    uint64_t pp = ffma2(fr, f2pack(0.05500892922282219f, 0.05500892922282219f),
+                        f2pack(0.2422109693288803f, 0.2422109693288803f));
+    pp = ffma2(pp, fr, f2pack(0.6932829022407532f, 0.6932829022407532f));
+    pp = ffma2(pp, fr, f2pack(1.f, 1.f));
+    float p0, p1, t0, t1;
+    f2unpack(pp, p0, p1);
+    f2unpack(t2, t0, t1);
+    // low bits of t hold round(x) (two's complement); << 23 moves it into the exponent
+    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 // p = 2^(s*scale - m) for 32 scores, packed to 16-bit pairs; row sum accumulated
 // in two packed fp32 accumulators
 template <typename T, bool MASKED>
@@ -126,9 +176,15 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&u)[32], int nv, uint6
             x0 = e < nv ? x0 : -INFINITY;
             x1 = e + 1 < nv ? x1 : -INFINITY;
         }
-        float t0, t1;
+        float t0, t1, p0, p1;
         f2unpack(ffma2(f2pack(x0, x1), sl2x2, negm2), t0, t1);
-        const float p0 = fast_exp2(t0), p1 = fast_exp2(t1);
+        // unmasked tiles: 6 of every 16 pairs on the FMA pipe, the rest on MUFU
+        if (!MASKED && ((e >> 1) & 7) >= 5) {
+            exp2_poly2(t0, t1, p0, p1);
+        } else {
+            p0 = fast_exp2(t0);
+            p1 = fast_exp2(t1);
+        }
         sum[(e >> 1) & 1] = fadd2(sum[(e >> 1) & 1], f2pack(p0, p1));
         pk[e >> 1] = Elem<T>::pack2(p0, p1);
     }
@@ -144,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using Sm = PrefillSmem<D>;
     constexpr bool kBF16 = !std::is_same<T, __half>::value;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t bars[16];
+    __shared__ __align__(8) uint64_t bars[NUM_BARS];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
 
@@ -174,6 +230,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (rowsX[0] <= 0 && rowsX[1] <= 0) return;   // uniform: unit beyond this sequence
     const int N = max(nX[0], nX[1]);
     const int kvh = hX[0] / p.group;
+#ifdef TECOOPS_PREFILL_TRACE
+    if (threadIdx.x == 0) {
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        PTRACE(0, globaltimer_ns());
+        PTRACE(1, smid);
+        PTRACE(2, N);
+        PTRACE(3, clock64());
+    }
+#endif
 
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t sbase = (raw_base + 1023u) & ~1023u;
@@ -182,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
 
     // rows of a sub-tile that have no admissible key (q_len > kv_len) are written as zeros
-    if (warp >= 2) {
+    if (warp >= 2 && warp < 10) {
         const int X = (warp - 2) >> 2;
         const int r = 32 * (warp & 3) + lane;
         const int qs = warp_seq_start(p.q_seq_lens, b);
@@ -209,15 +275,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     volatile int *abortp = &abort_flag;
+    if (threadIdx.x == 0) PTRACE(4, clock64());
     const bool last_partial = N * kBN > S;   // last KV tile holds rows past kv_len
 
-    if (warp == 0) {
-        // ===================== TMA producer =====================
-        const int qs = warp_seq_start(p.q_seq_lens, b);
-        if (lane == 0) {
+    if (warp == 0 || warp == 10) {
+        // ===================== TMA producers: warp 0 -> Q and K, warp 10 -> V ==============
+        // Separate warps so that a K tile never waits behind the V ring (K stages free up
+        // after the S MMAs, V stages only after the PV MMAs).  Page ids of the next tile
+        // are fetched while the current tile's stage is awaited.
+        const bool isV = warp == 10;
+        if (!isV && lane == 0) {
+            const int qs = warp_seq_start_lane0(p.q_seq_lens, b);
             tma_prefetch_desc(&qmap);
             tma_prefetch_desc(&kmap);
-            tma_prefetch_desc(&vmap);
             uint32_t qbytes = 0;
 #pragma unroll
             for (int X = 0; X < 2; ++X)
@@ -232,49 +302,57 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 BAR(Q_FULL), hh * 64, hX[X], qs + q0X[X]);
             }
         }
+        if (isV && lane == 0) tma_prefetch_desc(&vmap);
+        const CUtensorMap *map = isV ? &vmap : &kmap;
+        const int nst = isV ? kVStages : kKStages;
+        const int full0 = isV ? V_FULL : K_FULL;
+        const int empty0 = isV ? V_EMPTY : K_EMPTY;
+        const uint32_t ring = sbase + (isV ? Sm::kV0 : Sm::kK0);
         const int rpb = p.rows_per_box;
         const int nbox = kBN / rpb;
         const int *bt = p.block_table + (int64_t)b * p.block_table_dim;
-        int issued[2] = {0, 0};
-        for (int j = 0; j < N; ++j) {
-            const int s = j & 1;
-            if (j >= 2 && !mbar_wait_bounded(BAR(KV_EMPTY + s), ((j >> 1) - 1) & 1, abortp,
-                                             p.dev_error, kSiteEmpty + j))
-                break;
-            int blk = p.num_pages, row = 0;
+        auto page_of = [&](int j, int &row) {
+            int blk = p.num_pages;
+            row = 0;
             if (lane < nbox) {
                 const int tok = j * kBN + lane * rpb;
                 const int pi = tok / p.block_size;
                 row = tok - pi * p.block_size;
                 if (tok < S && pi < p.block_table_dim) blk = __ldg(bt + pi);
-                if (blk < 0 || blk >= p.num_pages) blk = p.num_pages;   // out of range -> zeros
             }
-            if (lane == 0) {
-                mbar_arrive_expect_tx(BAR(K_FULL + s), Sm::kTileBytes);
-                mbar_arrive_expect_tx(BAR(V_FULL + s), Sm::kTileBytes);
-            }
+            return blk;
+        };
+        int issued = 0;
+        int row_next = 0;
+        int blk_next = page_of(0, row_next);
+        for (int j = 0; j < N; ++j) {
+            int blk = blk_next, row = row_next;
+            if (j + 1 < N) blk_next = page_of(j + 1, row_next);   // in flight during the wait
+            if (blk < 0 || blk >= p.num_pages) blk = p.num_pages;  // out of range -> zeros
+            const int st = j % nst;
+            if (j >= nst && !mbar_wait_bounded(BAR(empty0 + st), ((j / nst) - 1) & 1, abortp,
+                                               p.dev_error, kSiteEmpty + (isV ? 0x80 : 0) + j))
+                break;
+            if (lane == 0 && j < 8) PTRACE((isV ? 104 : 96) + j, clock64());
+            if (lane == 0) mbar_arrive_expect_tx(BAR(full0 + st), Sm::kTileBytes);
             __syncwarp();
             if (lane < nbox) {
-                const uint32_t kdst = sbase + Sm::kK0 + s * Sm::kTileBytes + lane * rpb * 128;
-                const uint32_t vdst = sbase + Sm::kV0 + s * Sm::kTileBytes + lane * rpb * 128;
+                const uint32_t dst = ring + st * Sm::kTileBytes + lane * rpb * 128;
 #pragma unroll
-                for (int hh = 0; hh < Sm::kHalves; ++hh) {
-                    tma_load_4d(kdst + hh * Sm::kHalfBytes, &kmap, BAR(K_FULL + s), hh * 64, row,
-                                kvh, blk);
-                    tma_load_4d(vdst + hh * Sm::kHalfBytes, &vmap, BAR(V_FULL + s), hh * 64, row,
-                                kvh, blk);
-                }
+                for (int hh = 0; hh < Sm::kHalves; ++hh)
+                    tma_load_4d(dst + hh * Sm::kHalfBytes, map, BAR(full0 + st), hh * 64, row, kvh,
+                                blk);
             }
-            issued[s] = j + 1;
+            issued = j + 1;
         }
         // rows of the last V tile past kv_len may hold arbitrary bits (unwritten cache
         // slots): zero them before the PV MMAs of that tile read them
-        if (last_partial && issued[(N - 1) & 1] == N) {
-            const int s = (N - 1) & 1;
-            if (mbar_wait_bounded(BAR(V_FULL + s), ((N - 1) >> 1) & 1, abortp, p.dev_error,
+        if (isV && last_partial && issued == N) {
+            const int vs = (N - 1) % kVStages;
+            if (mbar_wait_bounded(BAR(V_FULL + vs), ((N - 1) / kVStages) & 1, abortp, p.dev_error,
                                   kSiteVz)) {
                 const int first = S - (N - 1) * kBN;   // first row to clear
-                uint8_t *vt = sgen + Sm::kV0 + s * Sm::kTileBytes;
+                uint8_t *vt = sgen + Sm::kV0 + vs * Sm::kTileBytes;
                 for (int r = first + lane; r < kBN; r += 32) {
 #pragma unroll
                     for (int hh = 0; hh < Sm::kHalves; ++hh) {
@@ -290,22 +368,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // on abort: let this warp's own copies in flight land before the CTA exits
         if (*abortp && lane == 0) {
-            for (int s = 0; s < 2; ++s) {
-                if (issued[s] == 0) continue;
-                const int j = issued[s] - 1;
-                mbar_wait_bounded(BAR(K_FULL + s), (j >> 1) & 1, nullptr, nullptr, 0, 100000000ull);
-                mbar_wait_bounded(BAR(V_FULL + s), (j >> 1) & 1, nullptr, nullptr, 0, 100000000ull);
-            }
+            for (int j = issued - nst < 0 ? 0 : issued - nst; j < issued; ++j)
+                mbar_wait_bounded(BAR(full0 + j % nst), (j / nst) & 1, nullptr, nullptr, 0,
+                                  100000000ull);
         }
     } else if (warp == 1) {
+
         // ===================== MMA issuer (one thread) =====================
+        // Fixed issue order, one (PV_X(j), S_X(j+1)) pair per sub-tile and tile:
+        //   PV_A(j) S_A(j+1) | PV_B(j) S_B(j+1) | ...
+        // Every operand of a pair is waited for first, then its 16 MMAs go out
+        // back-to-back: the tcgen05 issue queue is only a few MMAs deep, so any
+        // bookkeeping between groups would leave the tensor pipe idle.
+        // S_X(j+1) must follow PV_X(j): P_X(j) lives in S_X's TMEM columns and the
+        // MMAs of one thread execute in order.
         if (lane == 0) {
             const uint32_t idesc_qk = idesc_f16(kBF16, false, kBM, kBN);
             const uint32_t idesc_pv = idesc_f16(kBF16, true, kBM, D);
             bool ok = mbar_wait_bounded(BAR(Q_FULL), 0, abortp, p.dev_error, kSiteQ);
-            tc_fence_after();
+            PTRACE(5, clock64());
+            const int nA = nX[0], nB = nX[1];
             auto issue_s = [&](int X, int j) {
-                const uint32_t kbase = sbase + Sm::kK0 + (j & 1) * Sm::kTileBytes;
+                const uint32_t kbase = sbase + Sm::kK0 + (j % kKStages) * Sm::kTileBytes;
                 const uint32_t qbase = sbase + Sm::kQ0 + X * Sm::kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
@@ -314,63 +398,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                               smem_desc_sw128(kbase + koff, 16, 1024), idesc_qk,
                               kk > 0 ? 1u : 0u);
                 }
-                tc_commit(BAR(S_FULL + X));
             };
-            auto wait_k = [&](int j) {
-                if (!mbar_wait_bounded(BAR(K_FULL + (j & 1)), (j >> 1) & 1, abortp, p.dev_error,
-                                       kSiteK + j))
-                    return false;
-                tc_fence_after();
-                return true;
+            auto issue_pv = [&](int X, int j) {
+                const uint32_t vbase = sbase + Sm::kV0 + (j % kVStages) * Sm::kTileBytes;
+#pragma unroll
+                for (int t = 0; t < kBN / 16; ++t)
+                    tc_mma_ts(tmem + kColO + X * 128, tmem + kColS + X * 128 + t * 8,
+                              smem_desc_sw128(vbase + t * 16 * 128, Sm::kHalfBytes, 1024),
+                              idesc_pv, (j > 0 || t > 0) ? 1u : 0u);
             };
+            auto wait_k = [&](int k) {
+                return mbar_wait_bounded(BAR(K_FULL + k % kKStages), (k / kKStages) & 1, abortp,
+                                         p.dev_error, kSiteK + k);
+            };
+            // prologue: S_A(0), S_B(0)
             if (ok) ok = wait_k(0);
             if (ok) {
-                if (nX[0] > 0) issue_s(0, 0);
-                if (nX[1] > 0) issue_s(1, 0);
-            }
-            for (int j = 0; ok && j < N; ++j) {
-                const int s = j & 1;
-                if (!mbar_wait_bounded(BAR(V_FULL + s), (j >> 1) & 1, abortp, p.dev_error,
-                                       kSiteV + j)) {
-                    ok = false;
-                    break;
-                }
-                if (j == N - 1 && last_partial &&
-                    !mbar_wait_bounded(BAR(V_ZERO), 0, abortp, p.dev_error, kSiteVz)) {
-                    ok = false;
-                    break;
-                }
-                bool next_k_ready = false;
+                tc_fence_after();
 #pragma unroll
                 for (int X = 0; X < 2; ++X) {
-                    if (j >= nX[X]) continue;
+                    if ((X ? nB : nA) == 0) continue;
+                    if (X == 0) PTRACE(64, clock64());
+                    issue_s(X, 0);
+                    tc_commit(BAR(S_FULL + X));
+                }
+                tc_commit(BAR(K_EMPTY + 0));
+            }
+            for (int j = 0; ok && j < N; ++j) {
+                // V_j (and, for the last tile, the cleared tail rows) for both sub-tiles
+                if (j < 8) PTRACE(72 + j, clock64());
+                ok = mbar_wait_bounded(BAR(V_FULL + j % kVStages), (j / kVStages) & 1, abortp,
+                                       p.dev_error, kSiteV + j);
+                if (j < 8) PTRACE(80 + j, clock64());
+                if (ok && j == N - 1 && last_partial)
+                    ok = mbar_wait_bounded(BAR(V_ZERO), 0, abortp, p.dev_error, kSiteVz);
+                if (ok && j + 1 < N) ok = wait_k(j + 1);
+                if (j < 8) PTRACE(88 + j, clock64());
+                if (!ok) break;
+                if (j < 8) PTRACE(112 + j, clock64());
+#pragma unroll
+                for (int X = 0; X < 2; ++X) {
+                    const int n = X ? nB : nA;
+                    if (j >= n) continue;
                     if (!mbar_wait_bounded(BAR(P_FULL + X), j & 1, abortp, p.dev_error,
                                            kSiteP + j)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t vbase = sbase + Sm::kV0 + s * Sm::kTileBytes;
-#pragma unroll
-                    for (int t = 0; t < kBN / 16; ++t)
-                        tc_mma_ts(tmem + kColO + X * 128, tmem + kColS + X * 128 + t * 8,
-                                  smem_desc_sw128(vbase + t * 16 * 128, Sm::kHalfBytes, 1024),
-                                  idesc_pv, (j > 0 || t > 0) ? 1u : 0u);
-                    if (j + 1 < nX[X]) {
-                        if (!next_k_ready) {
-                            if (!wait_k(j + 1)) {
-                                ok = false;
-                                break;
-                            }
-                            next_k_ready = true;
-                        }
+                    if (j < 8) PTRACE(8 + 8 * X + j, clock64());
+                    issue_pv(X, j);
+                    if (j + 1 < n) {
                         issue_s(X, j + 1);
+                        tc_commit(BAR(S_FULL + X));
                     } else {
                         tc_commit(BAR(O_DONE + X));
                     }
+                    if (X == 0 && j < 8) PTRACE(120 + j, clock64());
                 }
                 if (!ok) break;
-                tc_commit(BAR(KV_EMPTY + s));
+                tc_commit(BAR(V_EMPTY + j % kVStages));
+                if (j + 1 < N) tc_commit(BAR(K_EMPTY + (j + 1) % kKStages));
             }
             // drain: every MMA issued by this thread has completed before TMEM is freed
             tc_commit(BAR(DRAIN));
@@ -403,26 +491,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
+            if ((warp & 3) == 2 && lane == 0 && j < 8) PTRACE(24 + 16 * X + j, clock64());
+#ifdef TECOOPS_TRACE_NOSOFTMAX
+            if (true) {   // diagnostic build only: measure the MMA / load pipeline alone
+                tc_fence_before();
+                mbar_arrive(BAR(P_FULL + X));
+                continue;
+            }
+#endif
             const int kbase = j * kBN;
             // columns kbase + c >= kbase + nvalid are masked (causal / kv_len tail)
             const int nvalid = klim - kbase + 1;
             const bool masked = __any_sync(0xffffffffu, nvalid < kBN);
-            // pass 1: row max over the 128 scores, two TMEM loads in flight per wait
+            // the whole 128-score row in registers: four loads, one wait
+            uint32_t u[4][32];
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, u[c]);
+            tmem_ld_wait();
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < kBN / 32; c += 2) {
-                uint32_t u0[32], u1[32];
-                tmem_ld32(tS + c * 32, u0);
-                tmem_ld32(tS + c * 32 + 32, u1);
-                tmem_ld_wait();
-                if (masked) {
-                    mx = chunk_max<true>(u0, nvalid - c * 32, mx);
-                    mx = chunk_max<true>(u1, nvalid - c * 32 - 32, mx);
-                } else {
-                    mx = chunk_max<false>(u0, 32, mx);
-                    mx = chunk_max<false>(u1, 32, mx);
-                }
-            }
+            for (int c = 0; c < kBN / 32; ++c)
+                mx = masked ? chunk_max<true>(u[c], nvalid - c * 32, mx)
+                            : chunk_max<false>(u[c], 32, mx);
             const float m_new = fmaxf(m_s, mx * sl2);
             const bool need = (j == 0) || (m_new > m_s + 8.0f);
             const bool warp_need = __any_sync(0xffffffffu, need);
@@ -432,20 +522,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_s = m_new;
             }
             const float m_use = (m_s == -INFINITY) ? 0.f : m_s;
-            // pass 2: p = 2^(s*scale - m), row sum, P (16-bit) written over the S columns
+            // p = 2^(s*scale - m), row sum, P (16-bit) written over the S columns
             const uint64_t sl2x2 = f2pack(sl2, sl2);
             const uint64_t negm2 = f2pack(-m_use, -m_use);
             uint64_t sum2[2] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
 #pragma unroll
             for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t u[32];
-                tmem_ld32(tS + c * 32, u);
-                tmem_ld_wait();
                 uint32_t pk[16];
                 if (masked)
-                    chunk_exp<T, true>(u, nvalid - c * 32, sl2x2, negm2, sum2, pk);
+                    chunk_exp<T, true>(u[c], nvalid - c * 32, sl2x2, negm2, sum2, pk);
                 else
-                    chunk_exp<T, false>(u, 32, sl2x2, negm2, sum2, pk);
+                    chunk_exp<T, false>(u[c], 32, sl2x2, negm2, sum2, pk);
                 tmem_st16(tS + c * 16, pk);
             }
             float s0, s1, s2, s3;
@@ -467,6 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tmem_st_wait();
             tc_fence_before();
+            if ((warp & 3) == 2 && lane == 0 && j < 8) PTRACE(32 + 16 * X + j, clock64());
             mbar_arrive(BAR(P_FULL + X));
         }
         // epilogue
@@ -500,11 +588,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) PTRACE(57, clock64());
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
 }
+
+#ifdef TECOOPS_PREFILL_TRACE
+extern "C" int tecoops_prefill_trace_read(long long *host, size_t n) {
+    return (int)cudaMemcpyFromSymbol(host, g_prefill_trace, n * sizeof(long long));
+}
+#endif
 
 // ---- host side ------------------------------------------------------------------------
 

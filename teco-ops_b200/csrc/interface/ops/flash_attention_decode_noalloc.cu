@@ -138,6 +138,7 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
     p.scale_log2 = (float)(1.0 / std::sqrt((double)head_dim)) * 1.4426950408889634f;
     p.part_o = nullptr;
     p.part_lse = nullptr;
+    p.dev_error = nullptr;
     const size_t need =
         tecoops::kern::decode_workspace_bytes(batch, heads, head_dim, p.max_splits);
     if (need > kNoAllocScratchBytes) {

@@ -12,11 +12,15 @@
 //    a GQA group are packed into the 16 rows of one warp MMA tile so every K/V
 //    byte is read from HBM exactly once;
 //  * the KV range of a sequence is cut into splits of `split_tokens` so that even
-//    64 sequences fill 148 SMs; each CTA streams its pages through a 3-stage
-//    cp.async ring (64 tokens x K and V per stage, XOR-swizzled 16-byte chunks so
-//    ldmatrix is bank-conflict free), 4 warps each own 16 tokens of a stage;
-//  * QK^T and PV on the warp MMA (m16n8k16, fp32 accumulate), online softmax in
-//    registers in the exp2 domain, P kept in registers as the A operand;
+//    64 sequences fill 148 SMs;
+//  * warp 4 is a TMA producer: each 16-token page chunk of K and V is one box (per
+//    64 columns) of a 4-D tensor map over the paged cache, with the page id as a
+//    coordinate (out-of-range ids read as zeros) and 128-byte swizzle, into a
+//    12-stage mbarrier ring; block-table ids are fetched 32 chunks at a time;
+//  * warps 0-3 consume chunks round-robin: QK^T and PV on the warp MMA
+//    (m16n8k16, fp32 accumulate) fed by conflict-free ldmatrix on the swizzled
+//    tiles, online softmax in the exp2 domain with the O rescale skipped when no
+//    row max grows, P kept in registers as the A operand;
 //  * the 4 warps merge through shared memory; a sequence that needs one split
 //    writes its output directly, otherwise (O/l, log2-sum-exp) partials go to
 //    the workspace and fa_decode_merge combines them.
@@ -24,42 +28,51 @@
 
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include "ual/kernels/common.cuh"
 #include "ual/kernels/launchers.h"
+#include "ual/kernels/sm100_primitives.cuh"
+#include "ual/kernels/tensor_map.h"
 
 namespace tecoops {
 namespace kern {
 
 namespace {
 
-constexpr int kStageTokens = 64;   // tokens per pipeline stage (4 warps x 16)
-constexpr int kStages = 3;
-constexpr int kThreads = 128;
+constexpr int kChunk = 16;        // tokens per ring stage (one MMA n-tile pair)
+constexpr int kStages = 12;       // multiple of the 4 consumer warps
+constexpr int kConsumers = 4;
+constexpr int kThreads = 32 * (kConsumers + 1);
 
 template <int D>
 struct DecodeSmem {
-    static constexpr int kRowBytes = D * 2;
-    static constexpr int kTileBytes = kStageTokens * kRowBytes;   // one of K or V
+    static constexpr int kHalves = D / 64;
+    static constexpr int kHalfBytes = kChunk * 128;            // 16 rows x 64 columns
+    static constexpr int kTileBytes = kHalves * kHalfBytes;    // K or V of one chunk
     static constexpr int kStageBytes = 2 * kTileBytes;
-    static constexpr int kPipeBytes = kStages * kStageBytes;
+    static constexpr int kRingBytes = kStages * kStageBytes;
     static constexpr int kMergeBytes = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
-    static constexpr int kBytes = kPipeBytes > kMergeBytes ? kPipeBytes : kMergeBytes;
+    static constexpr int kBytes = (kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes) + 1024;
 };
 
-// byte offset of 16-byte chunk `ch` of row `r` inside a [64][D] tile
-template <int D>
-__device__ __forceinline__ uint32_t swz(int r, int ch) {
-    return (uint32_t)(r * (D * 2) + ((ch ^ (r & 7)) << 4));
+// byte offset of 16-byte column chunk `ch` (0..D/8-1) of row `r` in a 128B-swizzled
+// [16][D] tile stored as D/64 halves of 16 rows x 128 bytes
+__device__ __forceinline__ uint32_t swz128(int r, int ch) {
+    return (uint32_t)((ch >> 3) * (kChunk * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
 }  // namespace
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 2) fa_decode_splitkv_kernel(DecodeParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(kThreads, 2)
+    fa_decode_splitkv_kernel(const __grid_constant__ CUtensorMap kmap,
+                             const __grid_constant__ CUtensorMap vmap, DecodeParams p) {
+    using namespace sm100;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[2 * kStages];
+    __shared__ int abort_flag;
     using Sm = DecodeSmem<D>;
-    constexpr int kChunks = D / 8;   // 16-byte chunks per row
 
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / p.num_slices;
@@ -78,120 +91,160 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_splitkv_kernel(DecodePa
     const int kv_end = min(kv_len, kv_begin + p.split_tokens);
     const int qrow = warp_seq_start(p.q_seq_lens, b);   // q_len == 1 on this path
     if (qrow >= p.total_q) return;                      // lengths beyond q's rows
+    const int nch = kv_end > kv_begin ? (kv_end - kv_begin + kChunk - 1) / kChunk : 0;
 
-    const int head0 = kvh * p.group + slice * 16;              // first q head of this tile
-    const int rows = min(16, p.group - slice * 16);            // valid q heads
+    const int head0 = kvh * p.group + slice * 16;   // first q head of this tile
+    const int rows = min(16, p.group - slice * 16);  // valid q heads
 
-    // ---- Q fragments (A operand), rows >= `rows` are zero ---------------------
-    const int g = lane >> 2;
-    const int c = lane & 3;
-    uint32_t qa[D / 16][4];
-    {
-        const T *qbase = static_cast<const T *>(p.q) + ((int64_t)qrow * p.num_heads + head0) * D;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-            const int k0 = kk * 16 + 2 * c;
-            const uint32_t *r0 = reinterpret_cast<const uint32_t *>(qbase + (int64_t)g * D + k0);
-            const uint32_t *r1 =
-                reinterpret_cast<const uint32_t *>(qbase + (int64_t)(g + 8) * D + k0);
-            qa[kk][0] = g < rows ? __ldg(r0) : 0u;
-            qa[kk][1] = g + 8 < rows ? __ldg(r1) : 0u;
-            qa[kk][2] = g < rows ? __ldg(r0 + 4) : 0u;
-            qa[kk][3] = g + 8 < rows ? __ldg(r1 + 4) : 0u;
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t *sgen = smem_raw + (sbase - raw);
+    const uint32_t bar0 = smem_u32(&bars[0]);
+    auto FULL = [&](int s) { return bar0 + 8u * (uint32_t)s; };
+    auto EMPTY = [&](int s) { return bar0 + 8u * (uint32_t)(kStages + s); };
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(FULL(s), 1);
+            mbar_init(EMPTY(s), 1);
         }
+        mbar_fence_init();
     }
-
-    const T *kc = static_cast<const T *>(p.key_cache);
-    const T *vc = static_cast<const T *>(p.value_cache);
-    const int *bt = p.block_table + (int64_t)b * p.block_table_dim;
-    const int64_t page_stride = (int64_t)p.num_kv_heads * p.block_size * D;   // elements
-    const int64_t head_off = (int64_t)kvh * p.block_size * D;
-
-    const int n_iters = (kv_end - kv_begin + kStageTokens - 1) / kStageTokens;
-    const uint32_t smem_base = smem_u32(smem);
-
-    auto issue_stage = [&](int it) {
-        const int buf = it % kStages;
-        const uint32_t kdst = smem_base + buf * Sm::kStageBytes;
-        const uint32_t vdst = kdst + Sm::kTileBytes;
-        const int t0 = kv_begin + it * kStageTokens;
-#pragma unroll
-        for (int i = 0; i < (kStageTokens * kChunks) / kThreads; ++i) {
-            const int id = tid + i * kThreads;
-            const int r = id / kChunks;
-            const int ch = id - r * kChunks;
-            const int tok = t0 + r;
-            bool valid = tok < kv_end;
-            int64_t off = 0;
-            int blk = valid ? __ldg(bt + tok / p.block_size) : -1;
-            valid = valid && blk >= 0 && blk < p.num_pages;   // bad page ids read as zeros
-            if (valid) {
-                const int in_page = tok - (tok / p.block_size) * p.block_size;
-                off = (int64_t)blk * page_stride + head_off + (int64_t)in_page * D + ch * 8;
-            }
-            const int nbytes = valid ? 16 : 0;
-            cp_async16(kdst + swz<D>(r, ch), kc + off, nbytes);
-            cp_async16(vdst + swz<D>(r, ch), vc + off, nbytes);
-        }
-    };
-
-#pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
-        if (s < n_iters) issue_stage(s);
-        cp_async_commit();
-    }
+    __syncthreads();
+    volatile int *abortp = &abort_flag;
 
     float m_r[2] = {-INFINITY, -INFINITY};
     float l_r[2] = {0.f, 0.f};
     float o[D / 8][4];
 #pragma unroll
     for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    const int g = lane >> 2;
+    const int c = lane & 3;
 
-    const float sl2 = p.scale_log2;
-    const int mi = lane >> 3;   // ldmatrix matrix index of this lane's address
-    const int ri = lane & 7;
-
-    for (int it = 0; it < n_iters; ++it) {
-        if (it + kStages - 1 < n_iters) issue_stage(it + kStages - 1);
-        cp_async_commit();
-        cp_async_wait<kStages - 1>();
-        __syncthreads();
-
-        const int buf = it % kStages;
-        const uint32_t ktile = smem_base + buf * Sm::kStageBytes;
-        const uint32_t vtile = ktile + Sm::kTileBytes;
-        const int wrow = warp * 16;
-        const int tok_base = kv_begin + it * kStageTokens + wrow;
-
-        if (tok_base < kv_end) {
-            // S = Q K^T for this warp's 16 tokens: two n-tiles of 8 tokens
+    if (warp == kConsumers) {
+        // ===================== TMA producer =====================
+        if (lane == 0) {
+            tma_prefetch_desc(&kmap);
+            tma_prefetch_desc(&vmap);
+        }
+        const int *bt = p.block_table + (int64_t)b * p.block_table_dim;
+        bool ok = true;
+        for (int g0 = 0; ok && g0 < nch; g0 += 32) {
+            // page id and in-page row of chunk g0 + lane
+            int blk = p.num_pages, row = 0;
+            const int cc = g0 + lane;
+            if (cc < nch) {
+                const int tok = kv_begin + cc * kChunk;
+                const int pi = tok / p.block_size;
+                row = tok - pi * p.block_size;
+                if (pi < p.block_table_dim) blk = __ldg(bt + pi);
+                if (blk < 0 || blk >= p.num_pages) blk = p.num_pages;   // read as zeros
+            }
+            const int cnt = min(32, nch - g0);
+            for (int i = 0; i < cnt; ++i) {
+                const int ci = g0 + i;
+                const int bi = __shfl_sync(0xffffffffu, blk, i);
+                const int ri = __shfl_sync(0xffffffffu, row, i);
+                if (lane == 0) {
+                    const int st = ci % kStages;
+                    if (ci >= kStages &&
+                        !mbar_wait_bounded(EMPTY(st), ((ci / kStages) - 1) & 1, abortp, p.dev_error,
+                                           0x1100 + (ci & 0xff)))
+                        ok = false;
+                    if (ok) {
+                        mbar_arrive_expect_tx(FULL(st), Sm::kStageBytes);
+                        const uint32_t kd = sbase + st * Sm::kStageBytes;
+                        const uint32_t vd = kd + Sm::kTileBytes;
+#pragma unroll
+                        for (int hh = 0; hh < Sm::kHalves; ++hh) {
+                            tma_load_4d(kd + hh * Sm::kHalfBytes, &kmap, FULL(st), hh * 64, ri,
+                                        kvh, bi);
+                            tma_load_4d(vd + hh * Sm::kHalfBytes, &vmap, FULL(st), hh * 64, ri,
+                                        kvh, bi);
+                        }
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+            }
+        }
+        // on abort: wait (bounded) for this warp's copies still in flight
+        if (*abortp && lane == 0) {
+            for (int ci = nch - kStages < 0 ? 0 : nch - kStages; ci < nch; ++ci)
+                mbar_wait_bounded(FULL(ci % kStages), (ci / kStages) & 1, nullptr, nullptr, 0,
+                                  100000000ull);
+        }
+    } else {
+        // ===================== consumers =====================
+        uint32_t qa[D / 16][4];
+        {
+            const T *qbase =
+                static_cast<const T *>(p.q) + ((int64_t)qrow * p.num_heads + head0) * D;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const int k0 = kk * 16 + 2 * c;
+                const uint32_t *r0 =
+                    reinterpret_cast<const uint32_t *>(qbase + (int64_t)g * D + k0);
+                const uint32_t *r1 =
+                    reinterpret_cast<const uint32_t *>(qbase + (int64_t)(g + 8) * D + k0);
+                qa[kk][0] = g < rows ? __ldg(r0) : 0u;
+                qa[kk][1] = g + 8 < rows ? __ldg(r1) : 0u;
+                qa[kk][2] = g < rows ? __ldg(r0 + 4) : 0u;
+                qa[kk][3] = g + 8 < rows ? __ldg(r1 + 4) : 0u;
+            }
+        }
+        const float sl2 = p.scale_log2;
+        const int mi = lane >> 3;   // ldmatrix matrix index of this lane's address
+        const int ri = lane & 7;
+        for (int ci = warp; ci < nch; ci += kConsumers) {
+            const int st = ci % kStages;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(FULL(st), (ci / kStages) & 1, abortp,
+                                                           p.dev_error, 0x1200 + (ci & 0xff))))
+                break;
+            const uint32_t ktile = sbase + st * Sm::kStageBytes;
+            const uint32_t vtile = ktile + Sm::kTileBytes;
+            const int tok0 = kv_begin + ci * kChunk;
+            const int nv = kv_end - tok0;   // valid tokens in this chunk
+            if (nv < kChunk) {
+                // V rows past kv_len may hold arbitrary bits (unwritten slots): clear them
+                uint8_t *vt = sgen + (vtile - sbase);
+                for (int idx = lane; idx < (kChunk - nv) * (D / 8); idx += 32) {
+                    const int r = nv + idx / (D / 8);
+                    const int ch = idx % (D / 8);
+                    *reinterpret_cast<uint4 *>(vt + swz128(r, ch)) = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async_smem();   // ordered before TMA refills this stage
+                __syncwarp();
+            }
+            // S = Q K^T: two n-tiles of 8 tokens
             float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
                 uint32_t kb[4];
-                const int r = wrow + (mi >> 1) * 8 + ri;
-                ldmatrix_x4(kb, ktile + swz<D>(r, 2 * kk + (mi & 1)));
+                const int r = (mi >> 1) * 8 + ri;
+                ldmatrix_x4(kb, ktile + swz128(r, 2 * kk + (mi & 1)));
                 mma16816<T>(s[0], qa[kk], kb[0], kb[1]);
                 mma16816<T>(s[1], qa[kk], kb[2], kb[3]);
             }
-            // scale, mask the ragged tail, online softmax (rows g and g+8)
             float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int tok = tok_base + 8 * j + 2 * c + (e & 1);
-                    const float x = tok < kv_end ? s[j][e] * sl2 : -INFINITY;
+                    const int t = 8 * j + 2 * c + (e & 1);
+                    const float x = t < nv ? s[j][e] * sl2 : -INFINITY;
                     s[j][e] = x;
                     mx[e >> 1] = fmaxf(mx[e >> 1], x);
                 }
             }
-            float alpha[2], mu[2];
+            float mu[2], alpha[2];
+            bool grow = false;
 #pragma unroll
             for (int r2 = 0; r2 < 2; ++r2) {
                 mx[r2] = fmaxf(mx[r2], __shfl_xor_sync(0xffffffffu, mx[r2], 1));
                 mx[r2] = fmaxf(mx[r2], __shfl_xor_sync(0xffffffffu, mx[r2], 2));
                 const float m_new = fmaxf(m_r[r2], mx[r2]);
+                grow |= m_new > m_r[r2];
                 mu[r2] = m_new == -INFINITY ? 0.f : m_new;
                 alpha[r2] = fast_exp2(m_r[r2] - mu[r2]);
                 m_r[r2] = m_new;
@@ -208,54 +261,56 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_splitkv_kernel(DecodePa
             }
             l_r[0] = l_r[0] * alpha[0] + ps[0];
             l_r[1] = l_r[1] * alpha[1] + ps[1];
+            if (__any_sync(0xffffffffu, grow)) {   // skip the rescale when no max grew
 #pragma unroll
-            for (int n = 0; n < D / 8; ++n) {
-                o[n][0] *= alpha[0];
-                o[n][1] *= alpha[0];
-                o[n][2] *= alpha[1];
-                o[n][3] *= alpha[1];
+                for (int n = 0; n < D / 8; ++n) {
+                    o[n][0] *= alpha[0];
+                    o[n][1] *= alpha[0];
+                    o[n][2] *= alpha[1];
+                    o[n][3] *= alpha[1];
+                }
             }
             uint32_t pa[4];
             pa[0] = Elem<T>::pack2(s[0][0], s[0][1]);
             pa[1] = Elem<T>::pack2(s[0][2], s[0][3]);
             pa[2] = Elem<T>::pack2(s[1][0], s[1][1]);
             pa[3] = Elem<T>::pack2(s[1][2], s[1][3]);
-            // O += P V
 #pragma unroll
             for (int nn = 0; nn < D / 16; ++nn) {
                 uint32_t vb[4];
-                const int r = wrow + (mi & 1) * 8 + ri;
-                ldmatrix_x4_trans(vb, vtile + swz<D>(r, 2 * nn + (mi >> 1)));
+                const int r = (mi & 1) * 8 + ri;
+                ldmatrix_x4_trans(vb, vtile + swz128(r, 2 * nn + (mi >> 1)));
                 mma16816<T>(o[2 * nn], pa, vb[0], vb[1]);
                 mma16816<T>(o[2 * nn + 1], pa, vb[2], vb[3]);
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(EMPTY(st));
         }
-        __syncthreads();
+        l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
+        l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
+        l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
+        l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
     }
-    cp_async_wait<0>();
 
-    // ---- merge the 4 warps through shared memory ------------------------------
-    l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
-    l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
-    l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
-    l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
-
-    float *so = reinterpret_cast<float *>(smem);               // [4][16][D]
-    float *sml = so + 4 * 16 * D;                               // [4][16][2]
+    // ---- merge the 4 consumer warps through shared memory (the ring is idle now) ----
     __syncthreads();
+    float *so = reinterpret_cast<float *>(sgen);   // [4][16][D]
+    float *sml = so + 4 * 16 * D;                  // [4][16][2]
+    if (warp < kConsumers) {
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n) {
-        const int col = n * 8 + 2 * c;
-        so[(warp * 16 + g) * D + col] = o[n][0];
-        so[(warp * 16 + g) * D + col + 1] = o[n][1];
-        so[(warp * 16 + g + 8) * D + col] = o[n][2];
-        so[(warp * 16 + g + 8) * D + col + 1] = o[n][3];
-    }
-    if (c == 0) {
-        sml[(warp * 16 + g) * 2 + 0] = m_r[0];
-        sml[(warp * 16 + g) * 2 + 1] = l_r[0];
-        sml[(warp * 16 + g + 8) * 2 + 0] = m_r[1];
-        sml[(warp * 16 + g + 8) * 2 + 1] = l_r[1];
+        for (int n = 0; n < D / 8; ++n) {
+            const int col = n * 8 + 2 * c;
+            so[(warp * 16 + g) * D + col] = o[n][0];
+            so[(warp * 16 + g) * D + col + 1] = o[n][1];
+            so[(warp * 16 + g + 8) * D + col] = o[n][2];
+            so[(warp * 16 + g + 8) * D + col + 1] = o[n][3];
+        }
+        if (c == 0) {
+            sml[(warp * 16 + g) * 2 + 0] = m_r[0];
+            sml[(warp * 16 + g) * 2 + 1] = l_r[0];
+            sml[(warp * 16 + g + 8) * 2 + 0] = m_r[1];
+            sml[(warp * 16 + g + 8) * 2 + 1] = l_r[1];
+        }
     }
     __syncthreads();
 
@@ -328,11 +383,10 @@ void decode_plan(int num_sms, int batch, int kv_heads, int group, int max_k, int
     const int64_t work = (int64_t)batch * kv_heads * slices * (int64_t)(max_k > 0 ? max_k : 1);
     const int64_t target = (int64_t)num_sms * 2 * 8;   // ~8 waves of 2 CTAs per SM
     int64_t split = (work + target - 1) / target;
-    split = ((split + kStageTokens - 1) / kStageTokens) * kStageTokens;
+    split = ((split + 63) / 64) * 64;
     if (split < 256) split = 256;
-    const int64_t cap = ((int64_t)(max_k > 0 ? max_k : 1) + kStageTokens - 1) / kStageTokens *
-                        kStageTokens;
-    if (split > cap) split = cap < kStageTokens ? kStageTokens : cap;
+    const int64_t cap = ((int64_t)(max_k > 0 ? max_k : 1) + 63) / 64 * 64;
+    if (split > cap) split = cap < 64 ? 64 : cap;
     *split_tokens = (int)split;
     *max_splits = (int)(((max_k > 0 ? max_k : 1) + split - 1) / split);
 }
@@ -345,12 +399,19 @@ size_t decode_workspace_bytes(int batch, int num_heads, int head_dim, int max_sp
 
 template <typename T, int D>
 static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
+    const bool bf16 = !std::is_same<T, __half>::value;
+    CUtensorMap kmap, vmap;
+    if (!encode_cache_map(&kmap, p.key_cache, bf16, D, p.block_size, p.num_kv_heads,
+                          p.num_pages, kChunk) ||
+        !encode_cache_map(&vmap, p.value_cache, bf16, D, p.block_size, p.num_kv_heads,
+                          p.num_pages, kChunk))
+        return cudaErrorInvalidValue;
     const int smem = DecodeSmem<D>::kBytes;
     auto kfn = fa_decode_splitkv_kernel<T, D>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p.max_splits, p.num_kv_heads * p.num_slices, p.batch);
-    kfn<<<grid, kThreads, smem, stream>>>(p);
+    kfn<<<grid, kThreads, smem, stream>>>(kmap, vmap, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (p.max_splits > 1) {

@@ -64,6 +64,7 @@ struct DecodeParams {
     float scale_log2;
     float *part_o;      // [batch, Hq, max_splits, D]
     float *part_lse;    // [batch, Hq, max_splits]
+    int *dev_error;     // error word for bounded waits (may be null)
 };
 
 bool decode_supported(int head_dim, int block_size, int group);

@@ -64,6 +64,7 @@ static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
     p.part_o = nullptr;
     p.part_lse = nullptr;
+    p.dev_error = a.dev_error;
     if (p.max_splits > 1) {
         const size_t need = kern::decode_workspace_bytes(p.batch, p.num_heads, p.head_dim,
                                                          p.max_splits);

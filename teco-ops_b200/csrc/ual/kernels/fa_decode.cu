@@ -16,7 +16,8 @@
 //  * warp 4 is a TMA producer: each 16-token page chunk of K and V is one box (per
 //    64 columns) of a 4-D tensor map over the paged cache, with the page id as a
 //    coordinate (out-of-range ids read as zeros) and 128-byte swizzle, into a
-//    12-stage mbarrier ring; block-table ids are fetched 32 chunks at a time;
+//    8-stage mbarrier ring (3 CTAs per SM, so up to 24 pages of K and V in flight
+//    per SM); block-table ids are fetched 32 chunks at a time;
 //  * warps 0-3 consume chunks round-robin: QK^T and PV on the warp MMA
 //    (m16n8k16, fp32 accumulate) fed by conflict-free ldmatrix on the swizzled
 //    tiles, online softmax in the exp2 domain with the O rescale skipped when no
@@ -41,7 +42,7 @@ namespace kern {
 namespace {
 
 constexpr int kChunk = 16;        // tokens per ring stage (one MMA n-tile pair)
-constexpr int kStages = 12;       // multiple of the 4 consumer warps
+constexpr int kStages = 8;        // multiple of the 4 consumer warps
 constexpr int kConsumers = 4;
 constexpr int kThreads = 32 * (kConsumers + 1);
 
@@ -65,7 +66,7 @@ __device__ __forceinline__ uint32_t swz128(int r, int ch) {
 }  // namespace
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     fa_decode_splitkv_kernel(const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, DecodeParams p) {
     using namespace sm100;

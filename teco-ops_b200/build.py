@@ -116,7 +116,8 @@ def build_plugin() -> str:
     if _stale(PLUGIN, deps):
         _run(["g++", "-std=c++17", "-O2", "-shared", "-fPIC", *INCS,
               "-I" + os.path.join(CSRC, "plugin"), "-I" + CUDA_INC, "-o", PLUGIN, *srcs,
-              "-L" + OUT, "-lteco_ops", "-Wl,-rpath,$ORIGIN"])
+              "-L" + OUT, "-lteco_ops", "-L/usr/local/cuda/lib64", "-lcudart_static", "-ldl",
+              "-lrt", "-lpthread", "-Wl,-rpath,$ORIGIN", "-Wl,--no-undefined"])
     return PLUGIN
 
 

@@ -1,0 +1,97 @@
+// C entry points of the stand-in plugin host: what the Teco-Inference engine does
+// with a registered AbstractPluginOp (shape inference, then Enqueue on its stream),
+// exposed so that tests can drive the plugins without the engine.
+#include <plugin/register_op.h>
+
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+namespace {
+std::string g_last_error;
+
+TECO_INFER::OpAttr make_attr(int n_attr, const char *const *names, const long long *vals) {
+    TECO_INFER::OpAttr a;
+    for (int i = 0; i < n_attr; ++i) a.ints[names[i]] = vals[i];
+    return a;
+}
+
+std::vector<std::vector<int>> make_shapes(int n, const int *ranks, const int *dims_flat) {
+    std::vector<std::vector<int>> s(n);
+    int off = 0;
+    for (int i = 0; i < n; ++i) {
+        s[i].assign(dims_flat + off, dims_flat + off + ranks[i]);
+        off += ranks[i];
+    }
+    return s;
+}
+}  // namespace
+
+extern "C" {
+
+const char *teco_plugin_last_error() { return g_last_error.c_str(); }
+
+// Registered plugin ops with their declared inputs, "op:in1,in2;op2:..." (returns length).
+int teco_plugin_list(char *buf, int cap) {
+    std::string s;
+    for (auto &kv : TECO_INFER::plugin_specs()) {
+        if (!s.empty()) s += ";";
+        s += kv.first + ":";
+        for (size_t i = 0; i < kv.second.inputs.size(); ++i)
+            s += (i ? "," : "") + kv.second.inputs[i];
+    }
+    if (buf && cap > 0) {
+        std::strncpy(buf, s.c_str(), cap - 1);
+        buf[cap - 1] = 0;
+    }
+    return (int)s.size();
+}
+
+// InferOutputShape of output 0: returns 0 and fills out_rank / out_dims (<= 8 dims).
+int teco_plugin_infer(const char *op, int n_in, const int *ranks, const int *dims_flat,
+                      int n_attr, const char *const *attr_names, const long long *attr_vals,
+                      int *out_rank, int *out_dims) {
+    auto it = TECO_INFER::plugin_impls().find(op);
+    if (it == TECO_INFER::plugin_impls().end()) return -1;
+    try {
+        auto impl = it->second();
+        std::vector<std::vector<int>> outs(1);
+        impl->InferOutputShape(make_shapes(n_in, ranks, dims_flat), n_in, outs, 1,
+                               make_attr(n_attr, attr_names, attr_vals));
+        *out_rank = (int)outs[0].size();
+        for (int i = 0; i < *out_rank && i < 8; ++i) out_dims[i] = outs[0][i];
+        return 0;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return -2;
+    }
+}
+
+// Enqueue with named inputs on `stream` (a cudaStream_t).
+int teco_plugin_enqueue(const char *op, int n_in, const char *const *in_names,
+                        void *const *in_ptrs, const int *ranks, const int *dims_flat, int n_out,
+                        void *const *out_ptrs, int n_attr, const char *const *attr_names,
+                        const long long *attr_vals, void *stream) {
+    auto it = TECO_INFER::plugin_impls().find(op);
+    if (it == TECO_INFER::plugin_impls().end()) return -1;
+    try {
+        auto ctx = std::make_shared<TECO_INFER::ComputeContext>();
+        auto shapes = make_shapes(n_in, ranks, dims_flat);
+        for (int i = 0; i < n_in; ++i) {
+            ctx->inputs[in_names[i]] = in_ptrs[i];
+            ctx->shapes[in_names[i]] = shapes[i];
+        }
+        ctx->outputs.assign(out_ptrs, out_ptrs + n_out);
+        ctx->attr = make_attr(n_attr, attr_names, attr_vals);
+        ctx->stream = static_cast<cudaStream_t>(stream);
+        auto impl = it->second();
+        impl->Enqueue(ctx);
+        return 0;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return -2;
+    }
+}
+
+}  // extern "C"

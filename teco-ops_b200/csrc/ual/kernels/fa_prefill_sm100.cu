@@ -388,24 +388,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = mbar_wait_bounded(BAR(Q_FULL), 0, abortp, p.dev_error, kSiteQ);
             PTRACE(5, clock64());
             const int nA = nX[0], nB = nX[1];
+            // Descriptors are built once; per MMA only the start-address field (bits
+            // 0-13, address >> 4) advances by a compile-time offset.  Shared-memory
+            // addresses stay below 2^18 bytes, so the add never carries out of the field.
+            const uint64_t dq0 = smem_desc_sw128(sbase + Sm::kQ0, 16, 1024);
+            const uint64_t dk0 = smem_desc_sw128(sbase + Sm::kK0, 16, 1024);
+            const uint64_t dv0 = smem_desc_sw128(sbase + Sm::kV0, Sm::kHalfBytes, 1024);
+            const uint32_t tS0 = tmem + kColS, tO0 = tmem + kColO;
             auto issue_s = [&](int X, int j) {
-                const uint32_t kbase = sbase + Sm::kK0 + (j % kKStages) * Sm::kTileBytes;
-                const uint32_t qbase = sbase + Sm::kQ0 + X * Sm::kTileBytes;
+                const uint64_t dq = dq0 + (uint64_t)((X * Sm::kTileBytes) >> 4);
+                const uint64_t dk = dk0 + (uint64_t)(((j % kKStages) * Sm::kTileBytes) >> 4);
+                const uint32_t d = tS0 + X * 128;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t koff = (kk >> 2) * Sm::kHalfBytes + (kk & 3) * 32;
-                    tc_mma_ss(tmem + kColS + X * 128, smem_desc_sw128(qbase + koff, 16, 1024),
-                              smem_desc_sw128(kbase + koff, 16, 1024), idesc_qk,
-                              kk > 0 ? 1u : 0u);
+                    constexpr int kHalfShift = Sm::kHalfBytes >> 4;
+                    const uint64_t off = (uint64_t)((kk >> 2) * kHalfShift + (kk & 3) * 2);
+                    tc_mma_ss(d, dq + off, dk + off, idesc_qk, kk > 0 ? 1u : 0u);
                 }
             };
             auto issue_pv = [&](int X, int j) {
-                const uint32_t vbase = sbase + Sm::kV0 + (j % kVStages) * Sm::kTileBytes;
+                const uint64_t dv = dv0 + (uint64_t)(((j % kVStages) * Sm::kTileBytes) >> 4);
+                const uint32_t d = tO0 + X * 128, a = tS0 + X * 128;
 #pragma unroll
                 for (int t = 0; t < kBN / 16; ++t)
-                    tc_mma_ts(tmem + kColO + X * 128, tmem + kColS + X * 128 + t * 8,
-                              smem_desc_sw128(vbase + t * 16 * 128, Sm::kHalfBytes, 1024),
-                              idesc_pv, (j > 0 || t > 0) ? 1u : 0u);
+                    tc_mma_ts(d, a + t * 8, dv + (uint64_t)(t * 16 * 128 / 16), idesc_pv,
+                              (j > 0 || t > 0) ? 1u : 0u);
             };
             auto wait_k = [&](int k) {
                 return mbar_wait_bounded(BAR(K_FULL + k % kKStages), (k / kKStages) & 1, abortp,

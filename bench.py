@@ -423,6 +423,171 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+class Llama70B:
+    """BASELINE config 5, Llama-3-70B-shaped attention sharded by KV head: Hq 64, Hkv 8,
+    D 128, bf16, bs 16.  Prefill: 2 sequences of 8192 tokens (causal), K/V written by
+    reshape_and_cache into a contiguous cache.  Decode: 256 sequences with context
+    U{1024..32768} (seed 41), block tables from a random permutation of the page pool
+    (seed 42), plus reshape of the 256 new tokens.  Rank r of G owns KV heads
+    [r*8/G, (r+1)*8/G) (strong scaling, no collective)."""
+
+    HQ, HKV = 64, 8
+
+    def __init__(self, rank, world, with_decode=True):
+        import torch
+        from tecoops import capi, sharding
+        self.torch, self.capi = torch, capi
+        dev = torch.device("cuda", torch.cuda.current_device())
+        s = sharding.head_shard(self.HQ, self.HKV, world, rank)
+        self.hq, self.hkv = s.q_heads, s.kv_heads
+        bf = torch.bfloat16
+        g = torch.Generator(device=dev).manual_seed(40 + rank)
+        # ---- prefill
+        self.lens = [8192, 8192]
+        tot = sum(self.lens)
+        self.q = torch.randn(tot, self.hq, D, device=dev, dtype=bf, generator=g)
+        self.k = torch.randn(tot, self.hkv, D, device=dev, dtype=bf, generator=g)
+        self.v = torch.randn(tot, self.hkv, D, device=dev, dtype=bf, generator=g)
+        pages = [cdiv(l, BS) for l in self.lens]
+        self.nb = sum(pages)
+        bt = torch.zeros(2, max(pages), dtype=torch.int32)
+        bt[0, :pages[0]] = torch.arange(pages[0], dtype=torch.int32)
+        bt[1, :pages[1]] = torch.arange(pages[0], pages[0] + pages[1], dtype=torch.int32)
+        self.bt = bt.to(dev)
+        self.slot = torch.arange(tot, device=dev)
+        self.kc = torch.zeros(self.nb, self.hkv, BS, D, device=dev, dtype=bf)
+        self.vc = torch.zeros_like(self.kc)
+        self.qlens = torch.tensor(self.lens, dtype=torch.int32, device=dev)
+        self.out = torch.empty_like(self.q)
+        self.flops = attn_flops(self.lens, self.lens, hq=self.hq)
+        self.h = capi.Handle(torch.cuda.current_stream().cuda_stream)
+        self.d = (capi.Desc(capi.DATA_INT32, self.bt.shape), capi.Desc(capi.DATA_BFLOAT16, self.q.shape),
+                  capi.Desc(capi.DATA_BFLOAT16, self.kc.shape))
+        self.flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
+        if with_decode:
+            self._setup_decode(dev, rank)
+
+    def _setup_decode(self, dev, rank):
+        torch, capi = self.torch, self.capi
+        B = 256
+        ctx = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(41))
+        pages = cdiv(ctx + 1, BS).tolist()
+        pool = sum(pages) + 1024
+        perm = torch.randperm(pool, generator=torch.Generator().manual_seed(42)).to(torch.int32)
+        bt = torch.zeros(B, max(pages), dtype=torch.int32)
+        p0 = 0
+        for b in range(B):
+            bt[b, :pages[b]] = perm[p0:p0 + pages[b]]
+            p0 += pages[b]
+        g = torch.Generator(device=dev).manual_seed(4100 + rank)
+        bf = torch.bfloat16
+        self.dkc = torch.randn(pool, self.hkv, BS, D, device=dev, dtype=bf, generator=g)
+        self.dvc = torch.randn(pool, self.hkv, BS, D, device=dev, dtype=bf, generator=g)
+        self.dq = torch.randn(B, self.hq, D, device=dev, dtype=bf, generator=g)
+        self.dknew = torch.randn(B, self.hkv, D, device=dev, dtype=bf, generator=g)
+        self.dvnew = torch.randn(B, self.hkv, D, device=dev, dtype=bf, generator=g)
+        slot = [int(bt[b, int(ctx[b]) // BS]) * BS + int(ctx[b]) % BS for b in range(B)]
+        self.dslot = torch.tensor(slot, dtype=torch.int64, device=dev)
+        self.dctx = (ctx + 1).to(torch.int32).to(dev)
+        self.dones = torch.ones(B, dtype=torch.int32, device=dev)
+        self.dbt = bt.to(dev)
+        self.dout = torch.empty_like(self.dq)
+        self.dd = (capi.Desc(capi.DATA_INT32, bt.shape), capi.Desc(capi.DATA_BFLOAT16, self.dq.shape),
+                   capi.Desc(capi.DATA_BFLOAT16, self.dkc.shape))
+        self.dB, self.dpool, self.dmaxk = B, pool, int(ctx.max()) + 1
+        self.dbytes = attn_bytes([1] * B, (ctx + 1).tolist(), hq=self.hq, hkv=self.hkv) + \
+            reshape_bytes(B, B, hkv=self.hkv)
+
+    def reshape(self):
+        tot = sum(self.lens)
+        self.capi.check(self.capi.reshape_and_cache(
+            self.h, self.k.data_ptr(), self.v.data_ptr(), self.slot.data_ptr(), self.kc.data_ptr(),
+            self.vc.data_ptr(), tot, self.hkv, D, self.nb, BS), "reshape")
+
+    def prefill(self):
+        b, q, c = self.d
+        self.capi.check(self.capi.flash_attention(
+            self.h, 8192, 8192, self.nb, self.qlens.data_ptr(), self.qlens.data_ptr(), b,
+            self.bt.data_ptr(), q, self.q.data_ptr(), c, self.kc.data_ptr(), c, self.vc.data_ptr(),
+            q, self.out.data_ptr()), "prefill")
+
+    def decode(self):
+        self.capi.check(self.capi.reshape_and_cache(
+            self.h, self.dknew.data_ptr(), self.dvnew.data_ptr(), self.dslot.data_ptr(),
+            self.dkc.data_ptr(), self.dvc.data_ptr(), self.dB, self.hkv, D, self.dpool, BS), "reshape")
+        b, q, c = self.dd
+        self.capi.check(self.capi.flash_attention(
+            self.h, 1, self.dmaxk, self.dpool, self.dones.data_ptr(), self.dctx.data_ptr(), b,
+            self.dbt.data_ptr(), q, self.dq.data_ptr(), c, self.dkc.data_ptr(), c,
+            self.dvc.data_ptr(), q, self.dout.data_ptr()), "decode")
+
+
+def run_70b(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    W = Llama70B(rank, world)
+    peaks, peak_src = load_peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    tr, tp = timed_loop(torch, args.steps, args.warmup, [W.reshape, W.prefill],
+                        flush=lambda: W.flush_buf.zero_())
+    barrier()
+    ms = max_over_ranks(sum(a + b for a, b in zip(tr, tp)))
+    total_flops = attn_flops(W.lens, W.lens, hq=Llama70B.HQ)
+    (td,) = timed_loop(torch, args.steps, args.warmup, [W.decode])
+    barrier()
+    dms = max_over_ranks(sum(td))
+    clk = clocks.stop()
+    kern_ms = sum(tp) / len(tp)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "prefill TFLOP/s", "value": args.steps * total_flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": "config 5: Llama-3-70B heads (Hq 64, Hkv 8, D 128), prefill "
+                                   "2 x 8192 causal (reshape + prefill per step), KV-head sharded",
+                       "parallelism": f"KV heads split over {world} GPUs, no collective",
+                       "l2": "flushed between timed prefill steps"},
+            "gpu_launches": 2 * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "fa_prefill_tcgen05_sm100",
+                         "achieved": W.flops / (kern_ms * 1e-3) / 1e12,
+                         "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": W.flops / (kern_ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
+                         "peak_source": f"{peak_src} bf16_tflops_sustained (long kernel)",
+                         "traffic": None},
+            "decode": {"workload": "config 5 decode: B 256, ctx U{1024..32768}, KV-head sharded",
+                       "metric": "decode HBM GB/s", "unit": "GB/s",
+                       "value": world * args.steps * W.dbytes / (dms * 1e-3) / 1e9,
+                       "ms_per_step": dms / args.steps,
+                       "per_gpu_frac_of_measured_hbm":
+                           args.steps * W.dbytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+            "clocks": clk}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_only(W, args, torch, rank):
     """One workload's timed loop (profiler captures run this)."""
     if args.only == "prefill":
@@ -556,6 +721,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--workload", choices=["config2", "70b"], default="config2",
+                    help="config2 (default headline, weak scaling) or 70b (config 5, "
+                         "KV-head sharded, strong scaling)")
     ap.add_argument("--only", choices=["prefill", "decode", "reshape"], default=None,
                     help="run one workload's timed loop only (for profiler captures); "
                          "prints a reduced JSON line")
@@ -564,6 +732,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "70b":
+        run_70b(args)
     else:
         run_ours(args)
 

@@ -175,3 +175,63 @@ def test_kv_head_shards_reassemble(name, world):
     got = torch.cat(parts, dim=1)
     mx, mean, _ = errors(got.float().cpu().numpy(), full.float().cpu().numpy())
     assert mx <= 2e-2 and mean <= 2e-3
+
+
+def test_config5_prefill_sampled_rows():
+    """BASELINE config 5 prefill (Hq 64, Hkv 8, 2 x 8192 causal) at full size; checked on
+    KV head 0's Q group for the last 256 rows of each sequence (they attend to all 8192
+    keys; the oracle treats them as a chunked prefill of 256 rows over 8192 keys)."""
+    from gpu_util import attention_capi, errors, reshape_capi
+    Hq, Hkv, D, bs, L = 64, 8, 128, 16, 8192
+    g = torch.Generator(device="cuda").manual_seed(40)
+    q = torch.randn(2 * L, Hq, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    k = torch.randn(2 * L, Hkv, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    v = torch.randn(2 * L, Hkv, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    nb = 2 * L // bs
+    kc = torch.zeros(nb, Hkv, bs, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    reshape_capi(k, v, torch.arange(2 * L, device="cuda"), kc, vc)
+    bt = torch.arange(nb, dtype=torch.int32).view(2, nb // 2)
+    lens = torch.tensor([L, L], dtype=torch.int32, device="cuda")
+    out = attention_capi(q, kc, vc, lens, lens, bt.cuda())
+    torch.cuda.synchronize()
+    for b in range(2):
+        rows = slice(b * L + L - 256, b * L + L)
+        ref = oracle.flash_attn_varlen(q[rows, 0:8].float().cpu().numpy(),
+                                       kc[:, 0:1].float().cpu().numpy(),
+                                       vc[:, 0:1].float().cpu().numpy(), [256], [L],
+                                       bt[b:b + 1].numpy())
+        mx, mean, diff1 = errors(out[rows, 0:8].float().cpu().numpy(), ref)
+        assert mx <= MAX_ABS and mean <= MEAN_ABS and diff1 <= DIFF1, (b, mx, mean, diff1)
+
+
+def test_config5_decode_sampled_sequences():
+    """BASELINE config 5 decode (B 256, ctx U{1024..32768}, Hq 64, Hkv 8) at full size on a
+    270k-page pool; 16 sequences checked against the oracle on a compacted pool."""
+    from gpu_util import attention_capi, errors
+    B, Hq, Hkv, D, bs = 256, 64, 8, 128, 16
+    ctx = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(41))
+    pages = ((ctx + bs - 1) // bs).tolist()
+    pool = sum(pages) + 1024
+    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(42)).to(torch.int32)
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    p0 = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[p0:p0 + pages[b]]
+        p0 += pages[b]
+    gd = torch.Generator(device="cuda").manual_seed(43)
+    kc = torch.randn(pool, Hkv, bs, D, device="cuda", dtype=torch.bfloat16, generator=gd)
+    vc = torch.randn(pool, Hkv, bs, D, device="cuda", dtype=torch.bfloat16, generator=gd)
+    q = torch.randn(B, Hq, D, device="cuda", dtype=torch.bfloat16, generator=gd)
+    out = attention_capi(q, kc, vc, torch.ones(B, dtype=torch.int32, device="cuda"),
+                         ctx.to(torch.int32).cuda(), bt.cuda(), max_q=1, max_k=int(ctx.max()))
+    torch.cuda.synchronize()
+    sample = torch.randperm(B, generator=torch.Generator().manual_seed(44))[:16].tolist()
+    for b in sample:
+        ids = bt[b, :pages[b]].long()
+        ref = oracle.flash_attn_varlen(q[b:b + 1].float().cpu().numpy(),
+                                       kc[ids.cuda()].float().cpu().numpy(),
+                                       vc[ids.cuda()].float().cpu().numpy(), [1], [int(ctx[b])],
+                                       np.arange(pages[b], dtype=np.int32)[None])
+        mx, mean, diff1 = errors(out[b:b + 1].float().cpu().numpy(), ref)
+        assert mx <= MAX_ABS and mean <= MEAN_ABS and diff1 <= DIFF1, (b, mx, mean, diff1)

@@ -21,7 +21,9 @@ struct tecoopsContext {
     // handle-owned scratch (grown on demand, freed by tecoopsDestroy)
     void *scratch = nullptr;
     size_t scratch_bytes = 0;
-    // one int of device memory that kernels set when a bounded wait gives up
+    // four ints of device memory: [0] error word that kernels set when a bounded wait
+    // gives up; [1], [2] the prefill kernel's work-unit and finished-CTA counters (zero
+    // between launches: the last CTA of each launch resets them)
     int *dev_error = nullptr;
 };
 

@@ -48,8 +48,8 @@ int *handleErrorWord(tecoopsContext *ctx) {
     cudaGetDevice(&prev);
     if (prev != ctx->device) cudaSetDevice(ctx->device);
     int *p = nullptr;
-    if (cudaMalloc(&p, sizeof(int)) == cudaSuccess) {
-        cudaMemset(p, 0, sizeof(int));
+    if (cudaMalloc(&p, 4 * sizeof(int)) == cudaSuccess) {
+        cudaMemset(p, 0, 4 * sizeof(int));
         ctx->dev_error = p;
     } else {
         cudaGetLastError();

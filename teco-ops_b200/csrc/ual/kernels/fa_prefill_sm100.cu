@@ -33,6 +33,12 @@
 //               the S columns it came from, lazy O rescale (only when the running max
 //               grows by more than 2^8), epilogue O / l -> global.
 // TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,256+D) O_1 [384,384+D).
+// Persistent: one CTA per SM walks work units (a Q row block of the two sub-tiles of
+// one sequence), heaviest first, drawn from a global counter; Q of the next unit is
+// loaded as soon as the current unit's last S MMAs have read Q, and its first PV
+// waits only for the previous epilogue to have read O out of TMEM, so consecutive
+// units overlap.  The counters live in the handle's device word block and are reset
+// by the last CTA to finish.
 // Every mbarrier wait is bounded (~2 s); a wait that gives up records its site in
 // the device error word and the CTA drains its MMAs, frees TMEM and exits.
 #include <cuda.h>
@@ -81,6 +87,7 @@ struct PrefillParams {
     const int *block_table;
     void *out;
     int *dev_error;
+    int *sched;         // [0] unit counter, [1] finished-CTA counter (zero at launch)
     int num_heads;
     int num_kv_heads;
     int group;
@@ -90,7 +97,8 @@ struct PrefillParams {
     int rows_per_box;   // min(block_size, 128)
     int block_table_dim;
     int num_pages;
-    int num_units;      // grid.z: q-tiles (pair_heads) or q-tile pairs
+    int num_units;      // per sequence: q-tiles (pair_heads) or q-tile pairs
+    int batch;
     int total_q;
     float scale_log2;
 };
@@ -112,13 +120,17 @@ __device__ long long g_prefill_trace[8192 * 128];
 
 enum WaitSite : int {
     kSiteQ = 0x100, kSiteK = 0x200, kSiteV = 0x300, kSiteEmpty = 0x400, kSiteS = 0x500,
-    kSiteP = 0x600, kSiteO = 0x700, kSiteDrain = 0x800, kSiteVz = 0x900
+    kSiteP = 0x600, kSiteO = 0x700, kSiteDrain = 0x800, kSiteVz = 0x900, kSiteSched = 0xa00
 };
 
 // barrier slots
 constexpr int kKStages = 3, kVStages = 2;
 constexpr int Q_FULL = 0, K_FULL = 1, K_EMPTY = 4, V_FULL = 7, V_EMPTY = 9, S_FULL = 11,
-              P_FULL = 13, O_DONE = 15, V_ZERO = 17, DRAIN = 18, NUM_BARS = 19;
+              P_FULL = 13, O_DONE = 15, V_ZERO = 17, DRAIN = 18, Q_EMPTY = 19, O_FREE = 20,
+              SCHED_FULL = 22, SCHED_EMPTY = 26, NUM_BARS = 30;
+// roles that take each work unit from the scheduler ring: the V producer, the MMA
+// thread and the 8 softmax warps (the Q/K producer is the scheduler)
+constexpr int kSchedConsumers = 10;
 
 // max of 32 scores (u) and acc; columns at or past `nv` are excluded when MASKED
 template <bool MASKED>
@@ -203,43 +215,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ __align__(8) uint64_t bars[NUM_BARS];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
+    // scheduler ring: {unit index, q_len, kv_len, first query row of the sequence}
+    __shared__ int4 sched_slot[4];
 
-    const int b = blockIdx.y;
-    const int unit = p.num_units - 1 - (int)blockIdx.z;   // heaviest units launch first
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-
-    const int L = __ldg(p.q_seq_lens + b);
-    const int S = __ldg(p.kv_seq_lens + b);
-    const int off = S - L;   // bottom-right causal offset: row i attends keys <= off + i
-    // the two sub-tiles of this CTA
-    int hX[2], q0X[2], rowsX[2], nX[2];
-#pragma unroll
-    for (int X = 0; X < 2; ++X) {
-        if (p.pair_heads) {
-            hX[X] = 2 * (int)blockIdx.x + X;
-            q0X[X] = unit * kBM;
-        } else {
-            hX[X] = (int)blockIdx.x;
-            q0X[X] = unit * 2 * kBM + X * kBM;
-        }
-        rowsX[X] = min(kBM, L - q0X[X]);
-        const int kv_hi = rowsX[X] > 0 ? min(S, off + q0X[X] + rowsX[X]) : 0;
-        nX[X] = (rowsX[X] > 0 && kv_hi > 0) ? (kv_hi + kBN - 1) / kBN : 0;
-    }
-    if (rowsX[0] <= 0 && rowsX[1] <= 0) return;   // uniform: unit beyond this sequence
-    const int N = max(nX[0], nX[1]);
-    const int kvh = hX[0] / p.group;
-#ifdef TECOOPS_PREFILL_TRACE
-    if (threadIdx.x == 0) {
-        unsigned smid;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        PTRACE(0, globaltimer_ns());
-        PTRACE(1, smid);
-        PTRACE(2, N);
-        PTRACE(3, clock64());
-    }
-#endif
 
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t sbase = (raw_base + 1023u) & ~1023u;
@@ -247,23 +227,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t bar0 = smem_u32(&bars[0]);
     auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
 
-    // rows of a sub-tile that have no admissible key (q_len > kv_len) are written as zeros
-    if (warp >= 2 && warp < 10) {
-        const int X = (warp - 2) >> 2;
-        const int r = 32 * (warp & 3) + lane;
-        const int qs = warp_seq_start(p.q_seq_lens, b);
-        const int nx = X ? nX[1] : nX[0], rx = X ? rowsX[1] : rowsX[0];
-        const int qx = X ? q0X[1] : q0X[0], hx = X ? hX[1] : hX[0];
-        if (nx == 0 && r < rx && qs + qx + r < p.total_q) {
-            T *o = static_cast<T *>(p.out) + ((int64_t)(qs + qx + r) * p.num_heads + hx) * D;
-            for (int d = 0; d < D; ++d) o[d] = Elem<T>::from_float(0.f);
-        }
-    }
-    if (N == 0) return;   // uniform
-
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int i = 0; i < NUM_BARS; ++i) mbar_init(BAR(i), (i == P_FULL || i == P_FULL + 1) ? 128 : 1);
+        for (int i = 0; i < NUM_BARS; ++i) {
+            const bool wg = i == P_FULL || i == P_FULL + 1 || i == O_FREE || i == O_FREE + 1;
+            const bool sched = i >= SCHED_EMPTY && i < SCHED_EMPTY + 4;
+            mbar_init(BAR(i), wg ? 128 : (sched ? kSchedConsumers : 1));
+        }
         mbar_fence_init();
     }
     if (warp == 1) {
@@ -275,34 +245,72 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     volatile int *abortp = &abort_flag;
-    if (threadIdx.x == 0) PTRACE(4, clock64());
-    const bool last_partial = N * kBN > S;   // last KV tile holds rows past kv_len
+
+    // Work units, heaviest first: index = ((u_from_top * batch) + b) * units_per_row + hp.
+    // CTA c starts on unit c; further units are handed out dynamically from
+    // gridDim.x + a global counter (p.sched[0]).  The Q/K producer warp draws them, skips
+    // empty units and publishes each with its sequence's lengths and first row through
+    // a 4-slot shared-memory ring (index -1 ends it); every other role takes the same
+    // sequence from the ring, so all barrier phases stay in step and only the producer
+    // reads the length arrays.
+    const int HP = p.pair_heads ? p.num_heads / 2 : p.num_heads;
+    const int total = p.num_units * p.batch * HP;
+    struct Unit {
+        int b, L, S, qs, off, kvh, N;
+        int hX[2], q0X[2], rowsX[2], nX[2];
+    };
+    auto read_slot = [&](int k) -> int4 {
+        const volatile int *v = reinterpret_cast<volatile int *>(&sched_slot[k & 3]);
+        return make_int4(v[0], v[1], v[2], v[3]);
+    };
+    // k-th unit of this CTA for a whole-warp consumer (lane 0 releases the slot)
+    auto take_unit_warp = [&](int k) -> int4 {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(SCHED_FULL + (k & 3)), (k >> 2) & 1,
+                                                       abortp, p.dev_error, kSiteSched)))
+            return make_int4(-1, 0, 0, 0);
+        const int4 e = read_slot(k);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(SCHED_EMPTY + (k & 3)));
+        return e;
+    };
+    // e = {index, q_len, kv_len, first row}
+    auto decode_unit = [&](int4 e, Unit &u) -> bool {
+        const int idx = e.x;
+        const int hp = idx % HP;
+        const int t = idx / HP;
+        u.b = t % p.batch;
+        const int unit = p.num_units - 1 - t / p.batch;
+        u.L = e.y;
+        u.S = e.z;
+        u.qs = e.w;
+        u.off = u.S - u.L;   // bottom-right causal: row i attends keys <= off + i
+#pragma unroll
+        for (int X = 0; X < 2; ++X) {
+            if (p.pair_heads) {
+                u.hX[X] = 2 * hp + X;
+                u.q0X[X] = unit * kBM;
+            } else {
+                u.hX[X] = hp;
+                u.q0X[X] = unit * 2 * kBM + X * kBM;
+            }
+            u.rowsX[X] = min(kBM, u.L - u.q0X[X]);
+            const int kv_hi = u.rowsX[X] > 0 ? min(u.S, u.off + u.q0X[X] + u.rowsX[X]) : 0;
+            u.nX[X] = (u.rowsX[X] > 0 && kv_hi > 0) ? (kv_hi + kBN - 1) / kBN : 0;
+        }
+        u.N = max(u.nX[0], u.nX[1]);
+        u.kvh = u.hX[0] / p.group;
+        return u.rowsX[0] > 0 || u.rowsX[1] > 0;
+    };
 
     if (warp == 0 || warp == 10) {
         // ===================== TMA producers: warp 0 -> Q and K, warp 10 -> V ==============
         // Separate warps so that a K tile never waits behind the V ring (K stages free up
         // after the S MMAs, V stages only after the PV MMAs).  Page ids of the next tile
-        // are fetched while the current tile's stage is awaited.
+        // are fetched while the current tile's stage is awaited.  Q of the next unit is
+        // loaded as soon as the last S MMA of the current unit has read Q.
         const bool isV = warp == 10;
-        if (!isV && lane == 0) {
-            const int qs = warp_seq_start_lane0(p.q_seq_lens, b);
-            tma_prefetch_desc(&qmap);
-            tma_prefetch_desc(&kmap);
-            uint32_t qbytes = 0;
-#pragma unroll
-            for (int X = 0; X < 2; ++X)
-                if (nX[X] > 0) qbytes += Sm::kTileBytes;
-            mbar_arrive_expect_tx(BAR(Q_FULL), qbytes);
-#pragma unroll
-            for (int X = 0; X < 2; ++X) {
-                if (nX[X] == 0) continue;
-#pragma unroll
-                for (int hh = 0; hh < Sm::kHalves; ++hh)
-                    tma_load_3d(sbase + Sm::kQ0 + X * Sm::kTileBytes + hh * Sm::kHalfBytes, &qmap,
-                                BAR(Q_FULL), hh * 64, hX[X], qs + q0X[X]);
-            }
-        }
-        if (isV && lane == 0) tma_prefetch_desc(&vmap);
+        if (lane == 0) tma_prefetch_desc(isV ? &vmap : &kmap);
+        if (!isV && lane == 0) tma_prefetch_desc(&qmap);
         const CUtensorMap *map = isV ? &vmap : &kmap;
         const int nst = isV ? kVStages : kKStages;
         const int full0 = isV ? V_FULL : K_FULL;
@@ -310,70 +318,138 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ring = sbase + (isV ? Sm::kV0 : Sm::kK0);
         const int rpb = p.rows_per_box;
         const int nbox = kBN / rpb;
-        const int *bt = p.block_table + (int64_t)b * p.block_table_dim;
-        auto page_of = [&](int j, int &row) {
-            int blk = p.num_pages;
-            row = 0;
-            if (lane < nbox) {
-                const int tok = j * kBN + lane * rpb;
-                const int pi = tok / p.block_size;
-                row = tok - pi * p.block_size;
-                if (tok < S && pi < p.block_table_dim) blk = __ldg(bt + pi);
+        int t_glob = 0;   // K or V tiles issued in this CTA
+        int units = 0;    // units with work seen so far
+        int zeroed = 0;   // last-tile clears done (V warp)
+        bool ok = true;
+        int next = blockIdx.x;   // next candidate unit (scheduler warp)
+        for (int k = 0; ok; ++k) {
+            int4 e;
+            if (!isV) {
+                // ===== scheduler: find the next non-empty unit and publish it =====
+                if (k >= 4)
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait_bounded(BAR(SCHED_EMPTY + (k & 3)),
+                                                      ((k >> 2) - 1) & 1, abortp, p.dev_error,
+                                                      kSiteSched));
+                e = make_int4(-1, 0, 0, 0);
+                for (int c = next; ok && c < total;) {
+                    const int b = (c / HP) % p.batch;
+                    const int L = __ldg(p.q_seq_lens + b);
+                    const int unit = p.num_units - 1 - c / (HP * p.batch);
+                    if (unit * (p.pair_heads ? kBM : 2 * kBM) < L) {
+                        e = make_int4(c, L, __ldg(p.kv_seq_lens + b),
+                                      warp_seq_start(p.q_seq_lens, b));
+                        break;
+                    }
+                    int d = 0;   // empty unit: draw another
+                    if (lane == 0) d = atomicAdd(p.sched, 1);
+                    c = (int)gridDim.x + __shfl_sync(0xffffffffu, d, 0);
+                }
+                if (lane == 0) {
+                    sched_slot[k & 3] = e;
+                    mbar_arrive(BAR(SCHED_FULL + (k & 3)));
+                    // the next draw is in flight while this unit's tiles are issued
+                    if (e.x >= 0) next = (int)gridDim.x + atomicAdd(p.sched, 1);
+                }
+                next = __shfl_sync(0xffffffffu, next, 0);
+            } else {
+                e = take_unit_warp(k);
             }
-            return blk;
-        };
-        int issued = 0;
-        int row_next = 0;
-        int blk_next = page_of(0, row_next);
-        for (int j = 0; j < N; ++j) {
-            int blk = blk_next, row = row_next;
-            if (j + 1 < N) blk_next = page_of(j + 1, row_next);   // in flight during the wait
-            if (blk < 0 || blk >= p.num_pages) blk = p.num_pages;  // out of range -> zeros
-            const int st = j % nst;
-            if (j >= nst && !mbar_wait_bounded(BAR(empty0 + st), ((j / nst) - 1) & 1, abortp,
-                                               p.dev_error, kSiteEmpty + (isV ? 0x80 : 0) + j))
-                break;
-            if (lane == 0 && j < 8) PTRACE((isV ? 104 : 96) + j, clock64());
-            if (lane == 0) mbar_arrive_expect_tx(BAR(full0 + st), Sm::kTileBytes);
-            __syncwarp();
-            if (lane < nbox) {
-                const uint32_t dst = ring + st * Sm::kTileBytes + lane * rpb * 128;
+            if (e.x < 0) break;
+            Unit u;
+            if (!decode_unit(e, u) || u.N == 0) continue;
+            const int qs = u.qs;
+            if (!isV && lane == 0) {
+                // Q buffers are free once the previous unit's last S MMAs completed
+                if (units > 0)
+                    ok = mbar_wait_bounded(BAR(Q_EMPTY), (units - 1) & 1, abortp, p.dev_error,
+                                           kSiteEmpty + 0xf0);
+                if (ok) {
+                    uint32_t qbytes = 0;
 #pragma unroll
-                for (int hh = 0; hh < Sm::kHalves; ++hh)
-                    tma_load_4d(dst + hh * Sm::kHalfBytes, map, BAR(full0 + st), hh * 64, row, kvh,
-                                blk);
-            }
-            issued = j + 1;
-        }
-        // rows of the last V tile past kv_len may hold arbitrary bits (unwritten cache
-        // slots): zero them before the PV MMAs of that tile read them
-        if (isV && last_partial && issued == N) {
-            const int vs = (N - 1) % kVStages;
-            if (mbar_wait_bounded(BAR(V_FULL + vs), ((N - 1) / kVStages) & 1, abortp, p.dev_error,
-                                  kSiteVz)) {
-                const int first = S - (N - 1) * kBN;   // first row to clear
-                uint8_t *vt = sgen + Sm::kV0 + vs * Sm::kTileBytes;
-                for (int r = first + lane; r < kBN; r += 32) {
+                    for (int X = 0; X < 2; ++X)
+                        if (u.nX[X] > 0) qbytes += Sm::kTileBytes;
+                    mbar_arrive_expect_tx(BAR(Q_FULL), qbytes);
 #pragma unroll
-                    for (int hh = 0; hh < Sm::kHalves; ++hh) {
-                        uint4 *q4 = reinterpret_cast<uint4 *>(vt + hh * Sm::kHalfBytes + r * 128);
+                    for (int X = 0; X < 2; ++X) {
+                        if (u.nX[X] == 0) continue;
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) q4[e] = make_uint4(0, 0, 0, 0);
+                        for (int hh = 0; hh < Sm::kHalves; ++hh)
+                            tma_load_3d(sbase + Sm::kQ0 + X * Sm::kTileBytes + hh * Sm::kHalfBytes,
+                                        &qmap, BAR(Q_FULL), hh * 64, u.hX[X], qs + u.q0X[X]);
                     }
                 }
-                fence_proxy_async_smem();
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            ++units;
+            const int *bt = p.block_table + (int64_t)u.b * p.block_table_dim;
+            auto page_of = [&](int j, int &row) {
+                int blk = p.num_pages;
+                row = 0;
+                if (lane < nbox) {
+                    const int tok = j * kBN + lane * rpb;
+                    const int pi = tok / p.block_size;
+                    row = tok - pi * p.block_size;
+                    if (tok < u.S && pi < p.block_table_dim) blk = __ldg(bt + pi);
+                }
+                return blk;
+            };
+            int row_next = 0;
+            int blk_next = page_of(0, row_next);
+            for (int j = 0; ok && j < u.N; ++j, ++t_glob) {
+                int blk = blk_next, row = row_next;
+                if (j + 1 < u.N) blk_next = page_of(j + 1, row_next);  // in flight during wait
+                if (blk < 0 || blk >= p.num_pages) blk = p.num_pages;   // out of range -> zeros
+                const int st = t_glob % nst;
+                if (t_glob >= nst)
+                    ok = mbar_wait_bounded(BAR(empty0 + st), ((t_glob / nst) - 1) & 1, abortp,
+                                           p.dev_error, kSiteEmpty + (isV ? 0x80 : 0));
+                if (!ok) break;
+                if (lane == 0) mbar_arrive_expect_tx(BAR(full0 + st), Sm::kTileBytes);
                 __syncwarp();
-                if (lane == 0) mbar_arrive(BAR(V_ZERO));
+                if (lane < nbox) {
+                    const uint32_t dst = ring + st * Sm::kTileBytes + lane * rpb * 128;
+#pragma unroll
+                    for (int hh = 0; hh < Sm::kHalves; ++hh)
+                        tma_load_4d(dst + hh * Sm::kHalfBytes, map, BAR(full0 + st), hh * 64,
+                                    row, u.kvh, blk);
+                }
+            }
+            // V rows of the unit's last tile past kv_len may hold arbitrary bits
+            // (unwritten cache slots): clear them before the PV MMAs of that tile
+            if (ok && isV && u.N * kBN > u.S) {
+                const int tl = t_glob - 1;
+                const int vs = tl % kVStages;
+                ok = mbar_wait_bounded(BAR(V_FULL + vs), (tl / kVStages) & 1, abortp,
+                                       p.dev_error, kSiteVz);
+                if (ok) {
+                    const int first = u.S - (u.N - 1) * kBN;
+                    uint8_t *vt = sgen + Sm::kV0 + vs * Sm::kTileBytes;
+                    for (int r = first + lane; r < kBN; r += 32) {
+#pragma unroll
+                        for (int hh = 0; hh < Sm::kHalves; ++hh) {
+                            uint4 *q4 =
+                                reinterpret_cast<uint4 *>(vt + hh * Sm::kHalfBytes + r * 128);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) q4[e] = make_uint4(0, 0, 0, 0);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(BAR(V_ZERO));
+                    ++zeroed;
+                }
             }
         }
         // on abort: let this warp's own copies in flight land before the CTA exits
         if (*abortp && lane == 0) {
-            for (int j = issued - nst < 0 ? 0 : issued - nst; j < issued; ++j)
-                mbar_wait_bounded(BAR(full0 + j % nst), (j / nst) & 1, nullptr, nullptr, 0,
+            for (int t = t_glob - nst < 0 ? 0 : t_glob - nst; t < t_glob; ++t)
+                mbar_wait_bounded(BAR(full0 + t % nst), (t / nst) & 1, nullptr, nullptr, 0,
                                   100000000ull);
         }
+        (void)zeroed;
     } else if (warp == 1) {
-
         // ===================== MMA issuer (one thread) =====================
         // Fixed issue order, one (PV_X(j), S_X(j+1)) pair per sub-tile and tile:
         //   PV_A(j) S_A(j+1) | PV_B(j) S_B(j+1) | ...
@@ -385,9 +461,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t idesc_qk = idesc_f16(kBF16, false, kBM, kBN);
             const uint32_t idesc_pv = idesc_f16(kBF16, true, kBM, D);
-            bool ok = mbar_wait_bounded(BAR(Q_FULL), 0, abortp, p.dev_error, kSiteQ);
-            PTRACE(5, clock64());
-            const int nA = nX[0], nB = nX[1];
             // Descriptors are built once; per MMA only the start-address field (bits
             // 0-13, address >> 4) advances by a compile-time offset.  Shared-memory
             // addresses stay below 2^18 bytes, so the add never carries out of the field.
@@ -395,9 +468,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t dk0 = smem_desc_sw128(sbase + Sm::kK0, 16, 1024);
             const uint64_t dv0 = smem_desc_sw128(sbase + Sm::kV0, Sm::kHalfBytes, 1024);
             const uint32_t tS0 = tmem + kColS, tO0 = tmem + kColO;
-            auto issue_s = [&](int X, int j) {
+            auto issue_s = [&](int X, int kt) {
                 const uint64_t dq = dq0 + (uint64_t)((X * Sm::kTileBytes) >> 4);
-                const uint64_t dk = dk0 + (uint64_t)(((j % kKStages) * Sm::kTileBytes) >> 4);
+                const uint64_t dk = dk0 + (uint64_t)(((kt % kKStages) * Sm::kTileBytes) >> 4);
                 const uint32_t d = tS0 + X * 128;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
@@ -406,66 +479,92 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_mma_ss(d, dq + off, dk + off, idesc_qk, kk > 0 ? 1u : 0u);
                 }
             };
-            auto issue_pv = [&](int X, int j) {
-                const uint64_t dv = dv0 + (uint64_t)(((j % kVStages) * Sm::kTileBytes) >> 4);
+            auto issue_pv = [&](int X, int vt, bool first) {
+                const uint64_t dv = dv0 + (uint64_t)(((vt % kVStages) * Sm::kTileBytes) >> 4);
                 const uint32_t d = tO0 + X * 128, a = tS0 + X * 128;
 #pragma unroll
                 for (int t = 0; t < kBN / 16; ++t)
                     tc_mma_ts(d, a + t * 8, dv + (uint64_t)(t * 16 * 128 / 16), idesc_pv,
-                              (j > 0 || t > 0) ? 1u : 0u);
+                              (!first || t > 0) ? 1u : 0u);
             };
-            auto wait_k = [&](int k) {
-                return mbar_wait_bounded(BAR(K_FULL + k % kKStages), (k / kKStages) & 1, abortp,
-                                         p.dev_error, kSiteK + k);
+            auto wait_k = [&](int kt) {
+                return mbar_wait_bounded(BAR(K_FULL + kt % kKStages), (kt / kKStages) & 1, abortp,
+                                         p.dev_error, kSiteK);
             };
-            // prologue: S_A(0), S_B(0)
-            if (ok) ok = wait_k(0);
-            if (ok) {
+            int kt = 0, vt = 0, units = 0, zeroed = 0;
+            int pcount[2] = {0, 0};   // P_X hand-offs consumed
+            int ounits[2] = {0, 0};   // units in which sub-tile X was active
+            bool ok = true;
+            for (int k = 0; ok; ++k) {
+                // k-th unit of this CTA (single-thread consumer of the scheduler ring)
+                if (!mbar_wait_bounded(BAR(SCHED_FULL + (k & 3)), (k >> 2) & 1, abortp,
+                                       p.dev_error, kSiteSched))
+                    break;
+                const int4 e = read_slot(k);
+                mbar_arrive(BAR(SCHED_EMPTY + (k & 3)));
+                if (e.x < 0) break;
+                Unit u;
+                if (!decode_unit(e, u) || u.N == 0) continue;
+                const bool partial = u.N * kBN > u.S;
+                ok = mbar_wait_bounded(BAR(Q_FULL), units & 1, abortp, p.dev_error, kSiteQ) &&
+                     wait_k(kt);
+                ++units;
+                if (!ok) break;
                 tc_fence_after();
+                // prologue: S_A(0), S_B(0)
 #pragma unroll
                 for (int X = 0; X < 2; ++X) {
-                    if ((X ? nB : nA) == 0) continue;
-                    if (X == 0) PTRACE(64, clock64());
-                    issue_s(X, 0);
+                    if (u.nX[X] == 0) continue;
+                    issue_s(X, kt);
                     tc_commit(BAR(S_FULL + X));
                 }
-                tc_commit(BAR(K_EMPTY + 0));
-            }
-            for (int j = 0; ok && j < N; ++j) {
-                // V_j (and, for the last tile, the cleared tail rows) for both sub-tiles
-                if (j < 8) PTRACE(72 + j, clock64());
-                ok = mbar_wait_bounded(BAR(V_FULL + j % kVStages), (j / kVStages) & 1, abortp,
-                                       p.dev_error, kSiteV + j);
-                if (j < 8) PTRACE(80 + j, clock64());
-                if (ok && j == N - 1 && last_partial)
-                    ok = mbar_wait_bounded(BAR(V_ZERO), 0, abortp, p.dev_error, kSiteVz);
-                if (ok && j + 1 < N) ok = wait_k(j + 1);
-                if (j < 8) PTRACE(88 + j, clock64());
-                if (!ok) break;
-                if (j < 8) PTRACE(112 + j, clock64());
+                tc_commit(BAR(K_EMPTY + kt % kKStages));
+                if (u.N == 1) tc_commit(BAR(Q_EMPTY));
+                for (int j = 0; ok && j < u.N; ++j) {
+                    const int vj = vt + j;   // V tile of unit tile j
+                    const int kn = kt + j + 1;   // K tile of unit tile j+1
+                    ok = mbar_wait_bounded(BAR(V_FULL + vj % kVStages), (vj / kVStages) & 1,
+                                           abortp, p.dev_error, kSiteV);
+                    if (ok && j == u.N - 1 && partial) {
+                        ok = mbar_wait_bounded(BAR(V_ZERO), zeroed & 1, abortp, p.dev_error,
+                                               kSiteVz);
+                        ++zeroed;
+                    }
+                    if (ok && j + 1 < u.N) ok = wait_k(kn);
+                    if (!ok) break;
 #pragma unroll
-                for (int X = 0; X < 2; ++X) {
-                    const int n = X ? nB : nA;
-                    if (j >= n) continue;
-                    if (!mbar_wait_bounded(BAR(P_FULL + X), j & 1, abortp, p.dev_error,
-                                           kSiteP + j)) {
-                        ok = false;
-                        break;
+                    for (int X = 0; X < 2; ++X) {
+                        const int n = u.nX[X];
+                        if (j >= n) continue;
+                        ok = mbar_wait_bounded(BAR(P_FULL + X), pcount[X] & 1, abortp,
+                                               p.dev_error, kSiteP);
+                        ++pcount[X];
+                        // the previous unit's epilogue must have read O_X before it is reset
+                        if (ok && j == 0 && ounits[X] > 0)
+                            ok = mbar_wait_bounded(BAR(O_FREE + X), (ounits[X] - 1) & 1, abortp,
+                                                   p.dev_error, kSiteO);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_pv(X, vj, j == 0);
+                        if (j + 1 < n) {
+                            issue_s(X, kn);
+                            tc_commit(BAR(S_FULL + X));
+                        } else {
+                            tc_commit(BAR(O_DONE + X));
+                        }
                     }
-                    tc_fence_after();
-                    if (j < 8) PTRACE(8 + 8 * X + j, clock64());
-                    issue_pv(X, j);
-                    if (j + 1 < n) {
-                        issue_s(X, j + 1);
-                        tc_commit(BAR(S_FULL + X));
-                    } else {
-                        tc_commit(BAR(O_DONE + X));
+                    if (!ok) break;
+                    tc_commit(BAR(V_EMPTY + vj % kVStages));
+                    if (j + 1 < u.N) {
+                        tc_commit(BAR(K_EMPTY + kn % kKStages));
+                        if (j + 2 == u.N) tc_commit(BAR(Q_EMPTY));   // last S of the unit
                     }
-                    if (X == 0 && j < 8) PTRACE(120 + j, clock64());
                 }
-                if (!ok) break;
-                tc_commit(BAR(V_EMPTY + j % kVStages));
-                if (j + 1 < N) tc_commit(BAR(K_EMPTY + (j + 1) % kKStages));
+#pragma unroll
+                for (int X = 0; X < 2; ++X)
+                    if (u.nX[X] > 0) ++ounits[X];
+                kt += u.N;
+                vt += u.N;
             }
             // drain: every MMA issued by this thread has completed before TMEM is freed
             tc_commit(BAR(DRAIN));
@@ -478,111 +577,124 @@ __global__ void __launch_bounds__(kThreads, 1)
         // TMEM lanes 32*(warp%4) .. +31, so row r = 32*(warp%4) + lane
         const int X = (warp - 2) >> 2;
         const int r = 32 * (warp & 3) + lane;
-        const int n = X ? nX[1] : nX[0];
-        const int rows = X ? rowsX[1] : rowsX[0];
-        const int hx = X ? hX[1] : hX[0];
         const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
         const uint32_t tS = tmem + lane_addr + kColS + X * 128;
         const uint32_t tO = tmem + lane_addr + kColO + X * 128;
-        const int qi = (X ? q0X[1] : q0X[0]) + r;
-        const int klim = min(off + qi, S - 1);   // last admissible key of this row
         const float sl2 = p.scale_log2;
-        const int qs = warp_seq_start(p.q_seq_lens, b);
-        float m_s = -INFINITY;   // running max, scaled (log2) units
-        float l = 0.f;
+        int scount = 0, ocount = 0;
         bool ok = true;
-        for (int j = 0; j < n; ++j) {
-            if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(S_FULL + X), j & 1, abortp,
-                                                           p.dev_error, kSiteS + j))) {
+        for (int k = 0; ok; ++k) {
+            const int4 e = take_unit_warp(k);
+            if (e.x < 0) break;
+            Unit u;
+            if (!decode_unit(e, u)) continue;
+            const int n = X ? u.nX[1] : u.nX[0];
+            const int rows = X ? u.rowsX[1] : u.rowsX[0];
+            const int hx = X ? u.hX[1] : u.hX[0];
+            const int qi = (X ? u.q0X[1] : u.q0X[0]) + r;
+            const int qs = u.qs;
+            if (n == 0) {
+                // rows with no admissible key (q_len > kv_len) are written as zeros
+                if (r < rows && qs + qi < p.total_q) {
+                    T *o = static_cast<T *>(p.out) + ((int64_t)(qs + qi) * p.num_heads + hx) * D;
+                    for (int d = 0; d < D; ++d) o[d] = Elem<T>::from_float(0.f);
+                }
+                continue;
+            }
+            const int klim = min(u.off + qi, u.S - 1);   // last admissible key of this row
+            float m_s = -INFINITY;   // running max, scaled (log2) units
+            float l = 0.f;
+            for (int j = 0; j < n; ++j) {
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(S_FULL + X), scount & 1,
+                                                               abortp, p.dev_error, kSiteS))) {
+                    ok = false;
+                    break;
+                }
+                ++scount;
+                tc_fence_after();
+                const int kbase = j * kBN;
+                // columns kbase + c >= kbase + nvalid are masked (causal / kv_len tail)
+                const int nvalid = klim - kbase + 1;
+                const bool masked = __any_sync(0xffffffffu, nvalid < kBN);
+                // the whole 128-score row in registers: four loads, one wait
+                uint32_t uu[4][32];
+#pragma unroll
+                for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, uu[c]);
+                tmem_ld_wait();
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < kBN / 32; ++c)
+                    mx = masked ? chunk_max<true>(uu[c], nvalid - c * 32, mx)
+                                : chunk_max<false>(uu[c], 32, mx);
+                const float m_new = fmaxf(m_s, mx * sl2);
+                const bool need = (j == 0) || (m_new > m_s + 8.0f);
+                const bool warp_need = __any_sync(0xffffffffu, need);
+                float alpha = 1.f;
+                if (warp_need) {
+                    alpha = (m_s == -INFINITY) ? 0.f : fast_exp2(m_s - m_new);
+                    m_s = m_new;
+                }
+                const float m_use = (m_s == -INFINITY) ? 0.f : m_s;
+                // p = 2^(s*scale - m), row sum, P (16-bit) written over the S columns
+                const uint64_t sl2x2 = f2pack(sl2, sl2);
+                const uint64_t negm2 = f2pack(-m_use, -m_use);
+                uint64_t sum2[2] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
+#pragma unroll
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t pk[16];
+                    if (masked)
+                        chunk_exp<T, true>(uu[c], nvalid - c * 32, sl2x2, negm2, sum2, pk);
+                    else
+                        chunk_exp<T, false>(uu[c], 32, sl2x2, negm2, sum2, pk);
+                    tmem_st16(tS + c * 16, pk);
+                }
+                float s0, s1, s2, s3;
+                f2unpack(sum2[0], s0, s1);
+                f2unpack(sum2[1], s2, s3);
+                l = l * alpha + ((s0 + s1) + (s2 + s3));
+                // O rescale: PV_X(j-1) has completed (S_X(j), issued after it, has)
+                if (j > 0 && warp_need) {
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t v[32];
+                        tmem_ld32(tO + c * 32, v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+                        tmem_st32(tO + c * 32, v);
+                    }
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(BAR(P_FULL + X));
+            }
+            if (!ok) break;
+            // epilogue; then hand O_X back for the next unit's first PV
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(O_DONE + X), ocount & 1, abortp,
+                                                           p.dev_error, kSiteO))) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            if ((warp & 3) == 2 && lane == 0 && j < 8) PTRACE(24 + 16 * X + j, clock64());
-#ifdef TECOOPS_TRACE_NOSOFTMAX
-            if (true) {   // diagnostic build only: measure the MMA / load pipeline alone
-                tc_fence_before();
-                mbar_arrive(BAR(P_FULL + X));
-                continue;
-            }
-#endif
-            const int kbase = j * kBN;
-            // columns kbase + c >= kbase + nvalid are masked (causal / kv_len tail)
-            const int nvalid = klim - kbase + 1;
-            const bool masked = __any_sync(0xffffffffu, nvalid < kBN);
-            // the whole 128-score row in registers: four loads, one wait
-            uint32_t u[4][32];
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, u[c]);
-            tmem_ld_wait();
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c)
-                mx = masked ? chunk_max<true>(u[c], nvalid - c * 32, mx)
-                            : chunk_max<false>(u[c], 32, mx);
-            const float m_new = fmaxf(m_s, mx * sl2);
-            const bool need = (j == 0) || (m_new > m_s + 8.0f);
-            const bool warp_need = __any_sync(0xffffffffu, need);
-            float alpha = 1.f;
-            if (warp_need) {
-                alpha = (m_s == -INFINITY) ? 0.f : fast_exp2(m_s - m_new);
-                m_s = m_new;
-            }
-            const float m_use = (m_s == -INFINITY) ? 0.f : m_s;
-            // p = 2^(s*scale - m), row sum, P (16-bit) written over the S columns
-            const uint64_t sl2x2 = f2pack(sl2, sl2);
-            const uint64_t negm2 = f2pack(-m_use, -m_use);
-            uint64_t sum2[2] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t pk[16];
-                if (masked)
-                    chunk_exp<T, true>(u[c], nvalid - c * 32, sl2x2, negm2, sum2, pk);
-                else
-                    chunk_exp<T, false>(u[c], 32, sl2x2, negm2, sum2, pk);
-                tmem_st16(tS + c * 16, pk);
-            }
-            float s0, s1, s2, s3;
-            f2unpack(sum2[0], s0, s1);
-            f2unpack(sum2[1], s2, s3);
-            l = l * alpha + ((s0 + s1) + (s2 + s3));
-            // O rescale: PV_{j-1} has completed (S_j, issued after it, has)
-            if (j > 0 && warp_need) {
-#pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    uint32_t u[32];
-                    tmem_ld32(tO + c * 32, u);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-                    tmem_st32(tO + c * 32, u);
-                }
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            if ((warp & 3) == 2 && lane == 0 && j < 8) PTRACE(32 + 16 * X + j, clock64());
-            mbar_arrive(BAR(P_FULL + X));
-        }
-        // epilogue
-        if (n > 0 &&
-            __all_sync(0xffffffffu, ok && mbar_wait_bounded(BAR(O_DONE + X), 0, abortp,
-                                                            p.dev_error, kSiteO + X))) {
+            ++ocount;
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             const bool store = r < rows && qs + qi < p.total_q;
             T *orow = static_cast<T *>(p.out) + ((int64_t)(qs + qi) * p.num_heads + hx) * D;
+            uint32_t ov[D / 32][32];
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                uint32_t u[32];
-                tmem_ld32(tO + c * 32, u);
-                tmem_ld_wait();
-                if (store) {
+            for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + c * 32, ov[c]);
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(BAR(O_FREE + X));
+            if (store) {
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
                     uint32_t pkd[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
-                        pkd[e] = Elem<T>::pack2(__uint_as_float(u[2 * e]) * inv,
-                                                __uint_as_float(u[2 * e + 1]) * inv);
+                        pkd[e] = Elem<T>::pack2(__uint_as_float(ov[c][2 * e]) * inv,
+                                                __uint_as_float(ov[c][2 * e + 1]) * inv);
                     uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
@@ -595,10 +707,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
-    if (threadIdx.x == 0) PTRACE(57, clock64());
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+    // the last CTA to finish resets the scheduler counters for the next launch
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+            atomicExch(p.sched, 0);
+            atomicExch(p.sched + 1, 0);
+        }
     }
 }
 
@@ -642,7 +761,9 @@ bool prefill_supported(int head_dim, int block_size, int group) {
 size_t prefill_workspace_bytes(const AttnShape &) { return 0; }
 
 template <typename T, int D>
-static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, cudaStream_t stream) {
+static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, int num_sms,
+                                   cudaStream_t stream) {
+    if (dev_error == nullptr) return cudaErrorInvalidValue;   // holds the scheduler counters
     PFN_encodeTiled enc = get_encode_fn();
     if (!enc) return cudaErrorNotSupported;
     const CUtensorMapDataType dt =
@@ -685,6 +806,7 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, cudaStre
     p.block_table = s.block_table;
     p.out = s.out;
     p.dev_error = dev_error;
+    p.sched = dev_error + 1;
     p.num_heads = s.num_heads;
     p.num_kv_heads = s.num_kv_heads;
     p.group = s.num_heads / s.num_kv_heads;
@@ -696,6 +818,7 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, cudaStre
     const int nqt = (s.max_q + kBM - 1) / kBM;
     p.num_units = p.pair_heads ? nqt : (nqt + 1) / 2;
     p.total_q = s.total_q;
+    p.batch = s.batch;
     p.scale_log2 = s.scale_log2;
     if (p.num_units <= 0 || s.batch <= 0) return cudaSuccess;
 
@@ -703,7 +826,10 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, cudaStre
     const int smem = PrefillSmem<D>::kAlloc;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.pair_heads ? s.num_heads / 2 : s.num_heads, s.batch, p.num_units);
+    const int units_total =
+        p.num_units * s.batch * (p.pair_heads ? s.num_heads / 2 : s.num_heads);
+    // persistent: one CTA per SM, units handed out by the in-kernel scheduler
+    dim3 grid(units_total < num_sms ? units_total : num_sms);
     kfn<<<grid, kThreads, smem, stream>>>(qmap, kmap, vmap, p);
     return cudaGetLastError();
 }
@@ -711,16 +837,15 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, cudaStre
 cudaError_t launch_prefill(const AttnShape &s, bool bf16, void *workspace, int *dev_error,
                            int num_sms, cudaStream_t stream) {
     (void)workspace;
-    (void)num_sms;
     const uintptr_t a = reinterpret_cast<uintptr_t>(s.q) | reinterpret_cast<uintptr_t>(s.key_cache) |
                         reinterpret_cast<uintptr_t>(s.value_cache);
     if (a & 15u) return cudaErrorMisalignedAddress;
     if (s.head_dim == 128)
-        return bf16 ? launch_prefill_t<__nv_bfloat16, 128>(s, dev_error, stream)
-                    : launch_prefill_t<__half, 128>(s, dev_error, stream);
+        return bf16 ? launch_prefill_t<__nv_bfloat16, 128>(s, dev_error, num_sms, stream)
+                    : launch_prefill_t<__half, 128>(s, dev_error, num_sms, stream);
     if (s.head_dim == 64)
-        return bf16 ? launch_prefill_t<__nv_bfloat16, 64>(s, dev_error, stream)
-                    : launch_prefill_t<__half, 64>(s, dev_error, stream);
+        return bf16 ? launch_prefill_t<__nv_bfloat16, 64>(s, dev_error, num_sms, stream)
+                    : launch_prefill_t<__half, 64>(s, dev_error, num_sms, stream);
     return cudaErrorInvalidValue;
 }
 

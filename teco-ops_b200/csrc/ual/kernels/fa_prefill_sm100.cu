@@ -245,6 +245,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     volatile int *abortp = &abort_flag;
+#ifdef TECOOPS_PREFILL_TRACE
+    if (threadIdx.x == 0) {
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        PTRACE(0, globaltimer_ns());
+        PTRACE(1, smid);
+        PTRACE(2, clock64());
+    }
+#endif
+#define UTRACE(k, e, v) \
+    do {                \
+        if ((k) < 7) PTRACE(8 + 16 * (k) + (e), (v)); \
+    } while (0)
 
     // Work units, heaviest first: index = ((u_from_top * batch) + b) * units_per_row + hp.
     // CTA c starts on unit c; further units are handed out dynamically from
@@ -506,8 +519,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 Unit u;
                 if (!decode_unit(e, u) || u.N == 0) continue;
                 const bool partial = u.N * kBN > u.S;
+                UTRACE(units, 0, clock64());
+                UTRACE(units, 7, u.N);
                 ok = mbar_wait_bounded(BAR(Q_FULL), units & 1, abortp, p.dev_error, kSiteQ) &&
                      wait_k(kt);
+                UTRACE(units, 1, clock64());
                 ++units;
                 if (!ok) break;
                 tc_fence_after();
@@ -544,6 +560,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = mbar_wait_bounded(BAR(O_FREE + X), (ounits[X] - 1) & 1, abortp,
                                                    p.dev_error, kSiteO);
                         if (!ok) break;
+                        if (X == 0 && j == 0) UTRACE(units - 1, 6, clock64());
+                        if (X == 0 && j + 1 == u.N) UTRACE(units - 1, 2, clock64());
                         tc_fence_after();
                         issue_pv(X, vj, j == 0);
                         if (j + 1 < n) {
@@ -602,6 +620,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 continue;
             }
             const int klim = min(u.off + qi, u.S - 1);   // last admissible key of this row
+#ifdef TECOOPS_PREFILL_TRACE
+            long long tr_busy = 0, tr_wait = 0, tr_prev = clock64(), tr_s = 0;
+#endif
             float m_s = -INFINITY;   // running max, scaled (log2) units
             float l = 0.f;
             for (int j = 0; j < n; ++j) {
@@ -611,6 +632,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 ++scount;
+                if (warp == 2 && lane == 0 && j == 0) UTRACE(ocount, 3, clock64());
+#ifdef TECOOPS_PREFILL_TRACE
+                tr_s = clock64();
+                if (j > 0) tr_wait += tr_s - tr_prev;
+#endif
                 tc_fence_after();
                 const int kbase = j * kBN;
                 // columns kbase + c >= kbase + nvalid are masked (causal / kv_len tail)
@@ -668,6 +694,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(BAR(P_FULL + X));
+#ifdef TECOOPS_PREFILL_TRACE
+                tr_prev = clock64();
+                tr_busy += tr_prev - tr_s;
+#endif
             }
             if (!ok) break;
             // epilogue; then hand O_X back for the next unit's first PV
@@ -675,6 +705,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                            p.dev_error, kSiteO))) {
                 ok = false;
                 break;
+            }
+            if (warp == 2 && lane == 0) {
+                UTRACE(ocount, 4, clock64());
+#ifdef TECOOPS_PREFILL_TRACE
+                UTRACE(ocount, 8, tr_busy);
+                UTRACE(ocount, 9, tr_wait);
+#endif
             }
             ++ocount;
             tc_fence_after();
@@ -702,11 +739,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                             pkd[4 * e + 3]);
                 }
             }
+            if (warp == 2 && lane == 0) UTRACE(ocount - 1, 5, clock64());
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) PTRACE(3, clock64());
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);

@@ -168,6 +168,48 @@ tecoopsStatus_t tecoopsFlashAttention(tecoopsHandle_t handle,
                                       void *oData, void *workspace);
 
 /*
+ * Extension: the flags the reference's Python binding accepts and ignores
+ * (api/torch_ext.cpp:99-113: softmax_scale, causal, window_size,
+ * return_softmax_lse), honoured.  For query row i of a sequence with q_len L
+ * and kv_len S (off = S - L), key j is admissible when
+ *   j <= off + i              (causal != 0; the reference's only mode)
+ *   j <= off + i + right      (causal == 0, window_right >= 0)
+ *   j >= off + i - left       (window_left >= 0)
+ * and j < S; negative window sides are unbounded (flash-attn convention).
+ * softmax_scale <= 0 selects 1/sqrt(head_size).  Rows with no admissible key
+ * are written as zeros (log-sum-exp -inf).
+ */
+typedef struct tecoopsFlashAttentionOptions {
+    float softmax_scale;
+    int causal;
+    int window_left;
+    int window_right;
+} tecoopsFlashAttentionOptions_t;
+
+/*
+ * tecoopsFlashAttention with options (nullptr = the reference's behaviour:
+ * causal, no window, scale 1/sqrt(head_size)) and an optional fp32 output
+ * softmax_lse [num_heads, sum(q_len)] of natural-log log-sum-exp values of the
+ * scaled, masked scores (nullptr: not written).  Same kernels and workspace.
+ */
+tecoopsStatus_t tecoopsFlashAttentionEx(tecoopsHandle_t handle,
+                                        int max_seqlen_q, int max_seqlen_k,
+                                        int max_block_num, const int *q_seq_lens,
+                                        const int *kv_seq_lens,
+                                        const tecoopsTensorDescriptor_t blockTableDesc,
+                                        const void *blockTable,
+                                        const tecoopsTensorDescriptor_t qDataDesc,
+                                        const void *qData,
+                                        const tecoopsTensorDescriptor_t kCacheDesc,
+                                        const void *kCache,
+                                        const tecoopsTensorDescriptor_t vCacheDesc,
+                                        const void *vCache,
+                                        const tecoopsTensorDescriptor_t oDataDesc,
+                                        void *oData, void *workspace,
+                                        const tecoopsFlashAttentionOptions_t *options,
+                                        float *softmax_lse);
+
+/*
  * Extension (no counterpart in the reference, whose `workspace` is always
  * nullptr): bytes of device scratch tecoopsFlashAttention needs for these
  * shapes, so that a caller can pass its own `workspace`.

@@ -15,6 +15,15 @@ python_api_test/test_flash_attention.py:49-110):
   py:125,134);
 * ``softmax(Q K^T * scale + bias) V`` in fp32 with scale ``1/sqrt(D)`` (py:127-137).
 
+Options beyond the reference (the flags its Python binding accepts and ignores,
+api/torch_ext.cpp:99-113): ``causal=False`` follows the golden's own ``causal``
+argument (no mask, py:112-116); ``window=(left, right)`` and the log-sum-exp
+output follow flash-attn's published definitions (key j admissible for row i when
+``S-L+i-left <= j <= S-L+i+right``, negative sides unbounded; lse = natural-log
+log-sum-exp of the scaled, masked scores, ``[Hq, total_q]``).  The reference has
+no window or lse, so those two are restated, not pinned to reference outputs.
+Rows with no admissible key give zeros (lse -inf).
+
 The golden's softmax is torch's (subtract the row max, exp, divide by the sum);
 numpy does the same in fp32.  The work is done one KV-head group at a time to
 bound memory (the math is unchanged).
@@ -30,13 +39,15 @@ def _cdiv(a: int, b: int) -> int:
     return (a + b - 1) // b
 
 
-def flash_attn_varlen(q, k_cache, v_cache, q_lens, kv_lens, block_table, softmax_scale=None):
+def flash_attn_varlen(q, k_cache, v_cache, q_lens, kv_lens, block_table, softmax_scale=None,
+                      causal=True, window=(-1, -1), return_lse=False):
     """Paged varlen causal GQA attention, fp32.
 
     q: float32 [total_q, Hq, D]; k_cache/v_cache: float32 [NB, Hkv, bs, D];
     q_lens/kv_lens: int sequences; block_table: int [B, bt_dim].
     Returns float32 [total_q, Hq, D] (rows outside every sequence stay 0, as the
-    golden's ``torch.zeros_like(q)``).
+    golden's ``torch.zeros_like(q)``), and with ``return_lse`` also float32
+    [Hq, total_q] log-sum-exp values (-inf where a row has no admissible key).
     """
     q = np.asarray(q, dtype=np.float32)
     k_cache = np.asarray(k_cache, dtype=np.float32)
@@ -47,6 +58,8 @@ def flash_attn_varlen(q, k_cache, v_cache, q_lens, kv_lens, block_table, softmax
     g = hq // hkv
     scale = 1.0 / math.sqrt(float(d)) if softmax_scale is None else float(softmax_scale)
     out = np.zeros_like(q)
+    lse = np.full((hq, q.shape[0]), -np.inf, dtype=np.float32)
+    wl, wr = int(window[0]), int(window[1])
     start = 0
     for b in range(len(q_lens)):
         L, S = int(q_lens[b]), int(kv_lens[b])
@@ -60,18 +73,33 @@ def flash_attn_varlen(q, k_cache, v_cache, q_lens, kv_lens, block_table, softmax
         v = v_cache[ids].transpose(0, 2, 1, 3).reshape(-1, hkv, d)[:S]
         i = np.arange(L)[:, None]
         j = np.arange(S)[None, :]
-        masked = j > (S - L + i)
+        if causal:
+            masked = j > (S - L + i)
+        elif wr >= 0:
+            masked = j > (S - L + i + wr)
+        else:
+            masked = np.zeros((L, S), dtype=bool)
+        if wl >= 0:
+            masked = masked | (j < (S - L + i - wl))
+        empty = masked.all(axis=1)                                         # [L]
         o = np.empty((L, hq, d), dtype=np.float32)
         for kv in range(hkv):
             qh = qs[:, kv * g:(kv + 1) * g, :].transpose(1, 0, 2)        # [g, L, D]
             s = np.matmul(qh, k[:, kv, :].T) * np.float32(scale)          # [g, L, S]
             s = np.where(masked[None], np.float32(-np.inf), s)
-            s = s - s.max(axis=-1, keepdims=True)
+            mx = s.max(axis=-1, keepdims=True) if S > 0 else np.zeros((g, L, 1), np.float32)
+            mx = np.where(np.isfinite(mx), mx, np.float32(0))
+            s = s - mx
             np.exp(s, out=s)
-            s /= s.sum(axis=-1, keepdims=True)
+            tot = s.sum(axis=-1, keepdims=True)
+            with np.errstate(divide="ignore"):
+                lse[kv * g:(kv + 1) * g, start - L:start] = np.where(
+                    tot[..., 0] > 0, np.log(tot[..., 0]) + mx[..., 0], -np.inf)
+            s /= np.where(tot > 0, tot, np.float32(1))
             o[:, kv * g:(kv + 1) * g, :] = np.matmul(s, v[:, kv, :]).transpose(1, 0, 2)
+        o[empty] = 0.0
         out[start - L:start] = o
-    return out
+    return (out, lse) if return_lse else out
 
 
 def causal_pairs(q_lens, kv_lens) -> int:

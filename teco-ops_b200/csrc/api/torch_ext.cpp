@@ -15,9 +15,12 @@
 //   * `out` is not zero-filled first: every row inside a sequence is written,
 //     rows past sum(q_lens) are left untouched; an undefined/empty `out` is
 //     allocated (zeros) and returned;
-//   * softmax_scale / causal / window_size / return_softmax_lse are accepted and
-//     ignored exactly like the reference (scale is always 1/sqrt(D), causal
-//     bottom-right masking always applies).
+//   * softmax_scale / causal / window_size / return_softmax_lse, which the
+//     reference accepts and ignores, are honoured through tecoopsFlashAttentionEx:
+//     softmax_scale <= 0 means 1/sqrt(D); window_size is empty or (left, right)
+//     with negative sides unbounded; return_softmax_lse returns (out, lse) with
+//     lse fp32 [Hq, total_q].  causal=True with the default scale reproduces the
+//     reference's (only) behaviour.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -111,7 +114,9 @@ void reshape_and_cache_torch(torch::Tensor key, torch::Tensor value, torch::Tens
 static torch::Tensor run_flash(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                torch::Tensor q_lens, torch::Tensor kv_lens,
                                torch::Tensor block_table, int64_t max_seqlen_q,
-                               int64_t max_seqlen_k, torch::Tensor out) {
+                               int64_t max_seqlen_k, torch::Tensor out,
+                               const tecoopsFlashAttentionOptions_t *opts = nullptr,
+                               float *lse = nullptr) {
     checkCuda(q, "q");
     checkCuda(k, "k_cache");
     checkCuda(v, "v_cache");
@@ -124,34 +129,47 @@ static torch::Tensor run_flash(torch::Tensor q, torch::Tensor k, torch::Tensor v
     c10::cuda::CUDAGuard g(q.device());
     tecoopsHandle_t h = handleFor(q.get_device());
     Desc bt(block_table), qd(q), kd(k), vd(v), od(out);
-    checkStatus(tecoopsFlashAttention(h, (int)max_seqlen_q, (int)max_seqlen_k, (int)k.size(0),
-                                      q_lens.data_ptr<int>(), kv_lens.data_ptr<int>(), bt.d,
-                                      block_table.data_ptr(), qd.d, q.data_ptr(), kd.d,
-                                      k.data_ptr(), vd.d, v.data_ptr(), od.d, out.data_ptr(),
-                                      nullptr),
+    checkStatus(tecoopsFlashAttentionEx(h, (int)max_seqlen_q, (int)max_seqlen_k, (int)k.size(0),
+                                        q_lens.data_ptr<int>(), kv_lens.data_ptr<int>(), bt.d,
+                                        block_table.data_ptr(), qd.d, q.data_ptr(), kd.d,
+                                        k.data_ptr(), vd.d, v.data_ptr(), od.d, out.data_ptr(),
+                                        nullptr, opts, lse),
                 "tecoopsFlashAttention");
     return out;
 }
 
-torch::Tensor flash_attn_varlen_func_torch(torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                                           int64_t max_seqlen_q, torch::Tensor cu_seqlens_q,
-                                           int64_t max_seqlen_k, torch::Tensor cu_seqlens_k,
-                                           torch::Tensor seqused_k, double softmax_scale,
-                                           bool causal, torch::Tensor window_size,
-                                           torch::Tensor block_table, bool return_softmax_lse,
-                                           torch::Tensor out) {
+pybind11::object flash_attn_varlen_func_torch(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                              int64_t max_seqlen_q, torch::Tensor cu_seqlens_q,
+                                              int64_t max_seqlen_k, torch::Tensor cu_seqlens_k,
+                                              torch::Tensor seqused_k, double softmax_scale,
+                                              bool causal, torch::Tensor window_size,
+                                              torch::Tensor block_table, bool return_softmax_lse,
+                                              torch::Tensor out) {
     (void)cu_seqlens_k;
-    (void)softmax_scale;
-    (void)causal;
-    (void)window_size;
-    (void)return_softmax_lse;
+    tecoopsFlashAttentionOptions_t opts;
+    opts.softmax_scale = softmax_scale > 0.0 ? (float)softmax_scale : 0.f;
+    opts.causal = causal ? 1 : 0;
+    opts.window_left = -1;
+    opts.window_right = -1;
+    if (window_size.defined() && window_size.numel() > 0) {
+        TORCH_CHECK(window_size.numel() == 2, "window_size must be empty or (left, right)");
+        auto w = window_size.to(torch::kCPU).to(torch::kLong);
+        opts.window_left = (int)w[0].item<int64_t>();
+        opts.window_right = (int)w[1].item<int64_t>();
+    }
     const int64_t batch = seqused_k.size(0);
     TORCH_CHECK(cu_seqlens_q.numel() >= batch + 1, "cu_seqlens_q must hold batch + 1 offsets");
     auto cu = cu_seqlens_q.to(at::kInt);
     // per-sequence query lengths, computed on the device (no host round trip)
     auto q_lens = (cu.slice(0, 1, batch + 1) - cu.slice(0, 0, batch)).contiguous();
     auto kv_lens = seqused_k.to(at::kInt).contiguous();
-    return run_flash(q, k, v, q_lens, kv_lens, block_table, max_seqlen_q, max_seqlen_k, out);
+    torch::Tensor lse;
+    if (return_softmax_lse)
+        lse = torch::full({q.size(1), q.size(0)}, -INFINITY, q.options().dtype(torch::kFloat));
+    auto o = run_flash(q, k, v, q_lens, kv_lens, block_table, max_seqlen_q, max_seqlen_k, out,
+                       &opts, return_softmax_lse ? lse.data_ptr<float>() : nullptr);
+    if (return_softmax_lse) return pybind11::make_tuple(o, lse);
+    return pybind11::cast(o);
 }
 
 // torch.ops.tecoops.* (C-API argument meaning: lengths, not offsets)

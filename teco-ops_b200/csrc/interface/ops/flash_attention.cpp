@@ -10,6 +10,8 @@
 //     non-packed strides and an INT32-less block table are rejected
 //     (BAD_PARAM / NOT_SUPPORTED) instead of reaching the kernel.
 //   - workspace == nullptr: the handle's own scratch is used (grown on demand).
+//   - tecoopsFlashAttentionEx: the same call with the binding's flags honoured
+//     (scale, causal, window) and an optional log-sum-exp output.
 #include <cmath>
 
 #include "interface/common/context.h"
@@ -90,6 +92,10 @@ static void fillArgs(FlashAttentionArgs &a, tecoopsHandle_t handle, int max_seql
     a.total_q = q->dimA[0];
     a.softmax_scale = (float)(1.0 / std::sqrt((double)a.size_per_head));
     a.dtype = k->dataType == TECOOPS_DATA_BFLOAT16 ? ElemType::BF16 : ElemType::F16;
+    a.causal = 1;
+    a.window_left = -1;
+    a.window_right = -1;
+    a.softmax_lse = nullptr;
 }
 
 extern "C" tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(
@@ -107,24 +113,33 @@ extern "C" tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(
     return TECOOPS_STATUS_SUCCESS;
 }
 
-extern "C" tecoopsStatus_t tecoopsFlashAttention(
-    tecoopsHandle_t handle, int max_seqlen_q, int max_seqlen_k, int max_block_num,
-    const int *q_seq_lens, const int *kv_seq_lens, const tecoopsTensorDescriptor_t blockTableDesc,
+static tecoopsStatus_t flashAttentionImpl(
+    tecoopsHandle_t handle, int max_seqlen_q, int max_seqlen_k, const int *q_seq_lens,
+    const int *kv_seq_lens, const tecoopsTensorDescriptor_t blockTableDesc,
     const void *blockTable, const tecoopsTensorDescriptor_t qDataDesc, const void *qData,
     const tecoopsTensorDescriptor_t kCacheDesc, const void *kCache,
     const tecoopsTensorDescriptor_t vCacheDesc, const void *vCache,
-    const tecoopsTensorDescriptor_t oDataDesc, void *oData, void *workspace) {
-    (void)max_block_num;   // the reference also takes the page count from kCacheDesc
+    const tecoopsTensorDescriptor_t oDataDesc, void *oData, void *workspace,
+    const tecoopsFlashAttentionOptions_t *options, float *softmax_lse) {
     tecoopsStatus_t st = flashAttentionCheckArgs(handle, blockTableDesc, qDataDesc, kCacheDesc,
                                                  vCacheDesc, oDataDesc);
     if (st != TECOOPS_STATUS_SUCCESS) return st;
     if (!q_seq_lens || !kv_seq_lens || !blockTable || !kCache || !vCache) return TECOOPS_STATUS_BAD_PARAM;
     if (qDataDesc->dimA[0] > 0 && (!qData || !oData)) return TECOOPS_STATUS_BAD_PARAM;
     if (max_seqlen_q < 0 || max_seqlen_k < 0) return TECOOPS_STATUS_BAD_PARAM;
+    if (options != nullptr && !(options->softmax_scale == options->softmax_scale))
+        return TECOOPS_STATUS_BAD_PARAM;   // NaN scale
     if (qDataDesc->dimA[0] == 0 || max_seqlen_q == 0) return TECOOPS_STATUS_SUCCESS;
 
     FlashAttentionArgs args{};
     fillArgs(args, handle, max_seqlen_q, max_seqlen_k, blockTableDesc, qDataDesc, kCacheDesc);
+    if (options != nullptr) {
+        if (options->softmax_scale > 0.f) args.softmax_scale = options->softmax_scale;
+        args.causal = options->causal != 0 ? 1 : 0;
+        args.window_left = options->window_left < 0 ? -1 : options->window_left;
+        args.window_right = options->window_right < 0 ? -1 : options->window_right;
+    }
+    args.softmax_lse = softmax_lse;
     args.q_seq_lens = q_seq_lens;
     args.kv_seq_lens = kv_seq_lens;
     args.block_table = static_cast<const int *>(blockTable);
@@ -146,4 +161,32 @@ extern "C" tecoopsStatus_t tecoopsFlashAttention(
     FlashAttentionPatchArgs patch{&args};
     TECOOPS_RUN_OP(FlashAttentionOp, args, patch, handle);
     return TECOOPS_STATUS_SUCCESS;
+}
+
+extern "C" tecoopsStatus_t tecoopsFlashAttention(
+    tecoopsHandle_t handle, int max_seqlen_q, int max_seqlen_k, int max_block_num,
+    const int *q_seq_lens, const int *kv_seq_lens, const tecoopsTensorDescriptor_t blockTableDesc,
+    const void *blockTable, const tecoopsTensorDescriptor_t qDataDesc, const void *qData,
+    const tecoopsTensorDescriptor_t kCacheDesc, const void *kCache,
+    const tecoopsTensorDescriptor_t vCacheDesc, const void *vCache,
+    const tecoopsTensorDescriptor_t oDataDesc, void *oData, void *workspace) {
+    (void)max_block_num;   // the reference also takes the page count from kCacheDesc
+    return flashAttentionImpl(handle, max_seqlen_q, max_seqlen_k, q_seq_lens, kv_seq_lens,
+                              blockTableDesc, blockTable, qDataDesc, qData, kCacheDesc, kCache,
+                              vCacheDesc, vCache, oDataDesc, oData, workspace, nullptr, nullptr);
+}
+
+extern "C" tecoopsStatus_t tecoopsFlashAttentionEx(
+    tecoopsHandle_t handle, int max_seqlen_q, int max_seqlen_k, int max_block_num,
+    const int *q_seq_lens, const int *kv_seq_lens, const tecoopsTensorDescriptor_t blockTableDesc,
+    const void *blockTable, const tecoopsTensorDescriptor_t qDataDesc, const void *qData,
+    const tecoopsTensorDescriptor_t kCacheDesc, const void *kCache,
+    const tecoopsTensorDescriptor_t vCacheDesc, const void *vCache,
+    const tecoopsTensorDescriptor_t oDataDesc, void *oData, void *workspace,
+    const tecoopsFlashAttentionOptions_t *options, float *softmax_lse) {
+    (void)max_block_num;
+    return flashAttentionImpl(handle, max_seqlen_q, max_seqlen_k, q_seq_lens, kv_seq_lens,
+                              blockTableDesc, blockTable, qDataDesc, qData, kCacheDesc, kCache,
+                              vCacheDesc, vCache, oDataDesc, oData, workspace, options,
+                              softmax_lse);
 }

@@ -139,6 +139,8 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
     p.part_o = nullptr;
     p.part_lse = nullptr;
     p.dev_error = nullptr;
+    p.window_left = -1;
+    p.lse = nullptr;
     const size_t need =
         tecoops::kern::decode_workspace_bytes(batch, heads, head_dim, p.max_splits);
     if (need > kNoAllocScratchBytes) {

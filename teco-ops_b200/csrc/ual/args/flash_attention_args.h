@@ -39,6 +39,11 @@ struct FlashAttentionArgs {
     void *workspace;         // device scratch (size from the op's workspaceSize)
     size_t workspace_bytes;
     int *dev_error;          // error word for bounded waits (may be null)
+    // options of tecoopsFlashAttentionEx (defaults: the reference's behaviour)
+    int causal;              // 1: bottom-right causal
+    int window_left;         // < 0: unbounded
+    int window_right;        // < 0: unbounded (ignored when causal)
+    float *softmax_lse;      // optional fp32 [Hq, total_q], natural log
 };
 
 // Branch selection input (reference FlashAttentionPatchArgs).

@@ -25,6 +25,9 @@
 //  * the 4 warps merge through shared memory; a sequence that needs one split
 //    writes its output directly, otherwise (O/l, log2-sum-exp) partials go to
 //    the workspace and fa_decode_merge combines them.
+//  * options: a left window (keys j >= kv_len - 1 - window_left) moves the first
+//    split to the window's 16-token chunk and masks the keys before it; the
+//    log-sum-exp (natural log) of each row is written when requested.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -86,9 +89,12 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int q_len = __ldg(p.q_seq_lens + b);
     const int kv_len = __ldg(p.kv_seq_lens + b);
     if (q_len <= 0) return;
-    const int kv_begin = split * p.split_tokens;
-    const int n_split_b = (kv_len + p.split_tokens - 1) / p.split_tokens;
-    if (kv_begin >= kv_len && !(split == 0 && kv_len <= 0)) return;
+    // first admissible key; splits start at its 16-token chunk (page-aligned boxes)
+    const int kv_lo = p.window_left >= 0 ? max(0, kv_len - 1 - p.window_left) : 0;
+    const int kv_base = kv_lo & ~(kChunk - 1);
+    const int kv_begin = kv_base + split * p.split_tokens;
+    const int n_split_b = (kv_len - kv_base + p.split_tokens - 1) / p.split_tokens;
+    if (kv_begin >= kv_len && !(split == 0 && kv_len - kv_base <= 0)) return;
     const int kv_end = min(kv_len, kv_begin + p.split_tokens);
     const int qrow = warp_seq_start(p.q_seq_lens, b);   // q_len == 1 on this path
     if (qrow >= p.total_q) return;                      // lengths beyond q's rows
@@ -205,7 +211,8 @@ __global__ void __launch_bounds__(kThreads, 3)
             const uint32_t ktile = sbase + st * Sm::kStageBytes;
             const uint32_t vtile = ktile + Sm::kTileBytes;
             const int tok0 = kv_begin + ci * kChunk;
-            const int nv = kv_end - tok0;   // valid tokens in this chunk
+            const int nv = kv_end - tok0;   // tokens of this chunk before kv_end
+            const int nlo = kv_lo - tok0;   // tokens of this chunk before the window
             if (nv < kChunk) {
                 // V rows past kv_len may hold arbitrary bits (unwritten slots): clear them
                 uint8_t *vt = sgen + (vtile - sbase);
@@ -233,7 +240,9 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int t = 8 * j + 2 * c + (e & 1);
-                    const float x = t < nv ? s[j][e] * sl2 : -INFINITY;
+                    // nlo <= t < nv as one unsigned compare (nlo < 16 <= ... and nv > nlo)
+                    const float x =
+                        (unsigned)(t - nlo) < (unsigned)(nv - nlo) ? s[j][e] * sl2 : -INFINITY;
                     s[j][e] = x;
                     mx[e >> 1] = fmaxf(mx[e >> 1], x);
                 }
@@ -335,6 +344,9 @@ __global__ void __launch_bounds__(kThreads, 3)
         if (direct) {
             T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * D + d;
             *out = Elem<T>::from_float(val);
+            if (p.lse != nullptr && d == 0)
+                p.lse[(int64_t)h * p.total_q + qrow] =
+                    L > 0.f ? (Mu + log2f(L)) * 0.6931471805599453f : -INFINITY;
         } else {
             const int64_t rec = ((int64_t)b * p.num_heads + h) * p.max_splits + split;
             p.part_o[rec * D + d] = val;
@@ -351,7 +363,8 @@ __global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
     const int h = blockIdx.x - b * p.num_heads;
     const int q_len = __ldg(p.q_seq_lens + b);
     const int kv_len = __ldg(p.kv_seq_lens + b);
-    const int ns = (kv_len + p.split_tokens - 1) / p.split_tokens;
+    const int kv_lo = p.window_left >= 0 ? max(0, kv_len - 1 - p.window_left) : 0;
+    const int ns = (kv_len - (kv_lo & ~15) + p.split_tokens - 1) / p.split_tokens;
     if (q_len <= 0 || ns <= 1) return;
     const int qrow = warp_seq_start(p.q_seq_lens, b);
     if (qrow >= p.total_q) return;
@@ -368,6 +381,9 @@ __global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
         }
         T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * p.head_dim + d;
         *out = Elem<T>::from_float(W > 0.f ? O / W : 0.f);
+        if (p.lse != nullptr && d == 0)
+            p.lse[(int64_t)h * p.total_q + qrow] =
+                W > 0.f ? (Mu + log2f(W)) * 0.6931471805599453f : -INFINITY;
     }
 }
 

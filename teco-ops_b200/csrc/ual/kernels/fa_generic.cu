@@ -9,7 +9,9 @@
 //
 // One warp per (query row, q head).  Keys are taken 32 at a time, one key per
 // lane for the dot product, then the lanes switch to owning head dimensions for
-// the P.V accumulation; online softmax in the exp2 domain.
+// the P.V accumulation; online softmax in the exp2 domain.  The options of
+// tecoopsFlashAttentionEx (scale, causal, window, log-sum-exp output) bound the
+// key range [lo, end) of each row.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -42,13 +44,17 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
     T *out = static_cast<T *>(s.out) + ((int64_t)row * s.num_heads + h) * D;
     if (b >= s.batch) {   // row beyond sum(q_seq_lens): leave zeros
         for (int d = lane; d < D; d += 32) out[d] = Elem<T>::from_float(0.f);
+        if (s.lse != nullptr && lane == 0) s.lse[(int64_t)h * s.total_q + row] = -INFINITY;
         return;
     }
     const int L = __ldg(s.q_seq_lens + b);
     const int S = __ldg(s.kv_seq_lens + b);
     const int i = row - start;
-    int allowed = S - L + i + 1;
-    if (allowed > S) allowed = S;
+    const int off = S - L;
+    // admissible keys [lo, end)
+    int end = s.causal ? off + i + 1 : (s.window_right >= 0 ? off + i + s.window_right + 1 : S);
+    if (end > S) end = S;
+    const int lo = s.window_left >= 0 ? max(0, off + i - s.window_left) : 0;
     const int kvh = h / (s.num_heads / s.num_kv_heads);
 
     const T *q = static_cast<const T *>(s.q) + ((int64_t)row * s.num_heads + h) * D;
@@ -66,11 +72,11 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
 #pragma unroll
     for (int k = 0; k < kMaxD / 32; ++k) acc[k] = 0.f;
 
-    for (int j0 = 0; j0 < allowed; j0 += 32) {
+    for (int j0 = lo; j0 < end; j0 += 32) {
         const int j = j0 + lane;
         float x = -INFINITY;
         int64_t my_off = 0;
-        if (j < allowed) {
+        if (j < end) {
             int blk = __ldg(bt + j / s.block_size);
             if (blk < 0 || blk >= s.num_pages) blk = 0;   // bad page id: stay in bounds
             my_off = (int64_t)blk * page_stride + head_off + (int64_t)(j % s.block_size) * D;
@@ -83,7 +89,7 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
         for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
         const float m_new = fmaxf(m, cm);
         const float alpha = exp2f(m - m_new);
-        const float pj = (j < allowed) ? exp2f(x - m_new) : 0.f;
+        const float pj = (j < end) ? exp2f(x - m_new) : 0.f;
         float ps = pj;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
@@ -91,7 +97,7 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
         m = m_new;
 #pragma unroll
         for (int k = 0; k < kMaxD / 32; ++k) acc[k] *= alpha;
-        const int nvalid = min(32, allowed - j0);
+        const int nvalid = min(32, end - j0);
         for (int t = 0; t < nvalid; ++t) {
             const float pt = __shfl_sync(0xffffffffu, pj, t);
             const int64_t off = __shfl_sync(0xffffffffu, my_off, t);
@@ -103,6 +109,9 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
         }
     }
     const float inv = l > 0.f ? 1.f / l : 0.f;
+    if (s.lse != nullptr && lane == 0)
+        s.lse[(int64_t)h * s.total_q + row] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f
+                                                      : -INFINITY;
 #pragma unroll
     for (int k = 0; k < kMaxD / 32; ++k) {
         const int d = lane + 32 * k;

@@ -101,6 +101,10 @@ struct PrefillParams {
     int batch;
     int total_q;
     float scale_log2;
+    int causal;         // key bounds of row i (off = kv_len - q_len): j < kv_len and
+    int window_left;    //   j <= off + i (causal) / off + i + window_right (non-causal,
+    int window_right;   //   right >= 0); j >= off + i - window_left (left >= 0)
+    float *lse;         // optional [Hq, total_q] natural-log log-sum-exp
 };
 
 #ifdef TECOOPS_PREFILL_TRACE
@@ -132,16 +136,18 @@ constexpr int Q_FULL = 0, K_FULL = 1, K_EMPTY = 4, V_FULL = 7, V_EMPTY = 9, S_FU
 // thread and the 8 softmax warps (the Q/K producer is the scheduler)
 constexpr int kSchedConsumers = 10;
 
-// max of 32 scores (u) and acc; columns at or past `nv` are excluded when MASKED
+// max of 32 scores (u) and acc; when MASKED only columns in [lo, nv) count
 template <bool MASKED>
-__device__ __forceinline__ float chunk_max(const uint32_t (&u)[32], int nv, float acc) {
+__device__ __forceinline__ float chunk_max(const uint32_t (&u)[32], int lo, int nv, float acc) {
     float m[4] = {acc, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int e = 0; e < 32; e += 2) {
         float x0 = __uint_as_float(u[e]), x1 = __uint_as_float(u[e + 1]);
         if (MASKED) {
-            x0 = e < nv ? x0 : -INFINITY;
-            x1 = e + 1 < nv ? x1 : -INFINITY;
+            // lo <= e < nv as one unsigned compare (an empty range masks everything)
+            const unsigned w = nv > lo ? (unsigned)(nv - lo) : 0u;
+            x0 = (unsigned)(e - lo) < w ? x0 : -INFINITY;
+            x1 = (unsigned)(e + 1 - lo) < w ? x1 : -INFINITY;
         }
         m[(e >> 1) & 3] = fmax3(m[(e >> 1) & 3], x0, x1);
     }
@@ -178,15 +184,17 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float 
 // p = 2^(s*scale - m) for 32 scores, packed to 16-bit pairs; row sum accumulated
 // in two packed fp32 accumulators
 template <typename T, bool MASKED>
-__device__ __forceinline__ void chunk_exp(const uint32_t (&u)[32], int nv, uint64_t sl2x2,
+__device__ __forceinline__ void chunk_exp(const uint32_t (&u)[32], int lo, int nv, uint64_t sl2x2,
                                           uint64_t negm2, uint64_t (&sum)[2],
                                           uint32_t (&pk)[16]) {
 #pragma unroll
     for (int e = 0; e < 32; e += 2) {
         float x0 = __uint_as_float(u[e]), x1 = __uint_as_float(u[e + 1]);
         if (MASKED) {
-            x0 = e < nv ? x0 : -INFINITY;
-            x1 = e + 1 < nv ? x1 : -INFINITY;
+            // lo <= e < nv as one unsigned compare (an empty range masks everything)
+            const unsigned w = nv > lo ? (unsigned)(nv - lo) : 0u;
+            x0 = (unsigned)(e - lo) < w ? x0 : -INFINITY;
+            x1 = (unsigned)(e + 1 - lo) < w ? x1 : -INFINITY;
         }
         float t0, t1, p0, p1;
         f2unpack(ffma2(f2pack(x0, x1), sl2x2, negm2), t0, t1);
@@ -204,7 +212,7 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&u)[32], int nv, uint6
 
 }  // namespace
 
-template <typename T, int D>
+template <typename T, int D, bool kWindow>   // kWindow: a left window bounds the keys
 __global__ void __launch_bounds__(kThreads, 1)
     fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap qmap,
                             const __grid_constant__ CUtensorMap kmap,
@@ -269,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int HP = p.pair_heads ? p.num_heads / 2 : p.num_heads;
     const int total = p.num_units * p.batch * HP;
     struct Unit {
-        int b, L, S, qs, off, kvh, N;
+        int b, L, S, qs, off, kvh, N, J0;   // KV tiles [J0, N) of the unit
         int hX[2], q0X[2], rowsX[2], nX[2];
     };
     auto read_slot = [&](int k) -> int4 {
@@ -307,10 +315,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 u.q0X[X] = unit * 2 * kBM + X * kBM;
             }
             u.rowsX[X] = min(kBM, u.L - u.q0X[X]);
-            const int kv_hi = u.rowsX[X] > 0 ? min(u.S, u.off + u.q0X[X] + u.rowsX[X]) : 0;
+            // one past the last admissible key of the sub-tile's last row
+            const int last = u.off + u.q0X[X] + u.rowsX[X] - 1;
+            const int kv_hi =
+                u.rowsX[X] > 0
+                    ? min(u.S, p.causal ? last + 1
+                                        : (p.window_right >= 0 ? last + p.window_right + 1 : u.S))
+                    : 0;
             u.nX[X] = (u.rowsX[X] > 0 && kv_hi > 0) ? (kv_hi + kBN - 1) / kBN : 0;
         }
         u.N = max(u.nX[0], u.nX[1]);
+        // first KV tile: the left window of the unit's first row (sub-tile 0's rows
+        // come first); every active sub-tile has tiles past it
+        u.J0 = kWindow ? max(0, u.off + u.q0X[0] - p.window_left) / kBN : 0;
+        if (u.J0 >= u.N) u.J0 = 0;
         u.kvh = u.hX[0] / p.group;
         return u.rowsX[0] > 0 || u.rowsX[1] > 0;
     };
@@ -409,8 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return blk;
             };
             int row_next = 0;
-            int blk_next = page_of(0, row_next);
-            for (int j = 0; ok && j < u.N; ++j, ++t_glob) {
+            int blk_next = page_of(u.J0, row_next);
+            for (int j = u.J0; ok && j < u.N; ++j, ++t_glob) {
                 int blk = blk_next, row = row_next;
                 if (j + 1 < u.N) blk_next = page_of(j + 1, row_next);  // in flight during wait
                 if (blk < 0 || blk >= p.num_pages) blk = p.num_pages;   // out of range -> zeros
@@ -535,10 +553,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_commit(BAR(S_FULL + X));
                 }
                 tc_commit(BAR(K_EMPTY + kt % kKStages));
-                if (u.N == 1) tc_commit(BAR(Q_EMPTY));
-                for (int j = 0; ok && j < u.N; ++j) {
-                    const int vj = vt + j;   // V tile of unit tile j
-                    const int kn = kt + j + 1;   // K tile of unit tile j+1
+                if (u.N - u.J0 == 1) tc_commit(BAR(Q_EMPTY));
+                for (int j = u.J0; ok && j < u.N; ++j) {
+                    const int vj = vt + (j - u.J0);       // V ring tile of unit tile j
+                    const int kn = kt + (j - u.J0) + 1;   // K ring tile of unit tile j+1
                     ok = mbar_wait_bounded(BAR(V_FULL + vj % kVStages), (vj / kVStages) & 1,
                                            abortp, p.dev_error, kSiteV);
                     if (ok && j == u.N - 1 && partial) {
@@ -556,14 +574,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                p.dev_error, kSiteP);
                         ++pcount[X];
                         // the previous unit's epilogue must have read O_X before it is reset
-                        if (ok && j == 0 && ounits[X] > 0)
+                        if (ok && j == u.J0 && ounits[X] > 0)
                             ok = mbar_wait_bounded(BAR(O_FREE + X), (ounits[X] - 1) & 1, abortp,
                                                    p.dev_error, kSiteO);
                         if (!ok) break;
-                        if (X == 0 && j == 0) UTRACE(units - 1, 6, clock64());
+                        if (X == 0 && j == u.J0) UTRACE(units - 1, 6, clock64());
                         if (X == 0 && j + 1 == u.N) UTRACE(units - 1, 2, clock64());
                         tc_fence_after();
-                        issue_pv(X, vj, j == 0);
+                        issue_pv(X, vj, j == u.J0);
                         if (j + 1 < n) {
                             issue_s(X, kn);
                             tc_commit(BAR(S_FULL + X));
@@ -581,8 +599,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int X = 0; X < 2; ++X)
                     if (u.nX[X] > 0) ++ounits[X];
-                kt += u.N;
-                vt += u.N;
+                kt += u.N - u.J0;
+                vt += u.N - u.J0;
             }
             // drain: every MMA issued by this thread has completed before TMEM is freed
             tc_commit(BAR(DRAIN));
@@ -616,32 +634,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (r < rows && qs + qi < p.total_q) {
                     T *o = static_cast<T *>(p.out) + ((int64_t)(qs + qi) * p.num_heads + hx) * D;
                     for (int d = 0; d < D; ++d) o[d] = Elem<T>::from_float(0.f);
+                    if (p.lse != nullptr) p.lse[(int64_t)hx * p.total_q + qs + qi] = -INFINITY;
                 }
                 continue;
             }
-            const int klim = min(u.off + qi, u.S - 1);   // last admissible key of this row
+            // admissible keys of this row: [klo, klim]
+            const int klim = min(p.causal ? u.off + qi
+                                          : (p.window_right >= 0 ? u.off + qi + p.window_right
+                                                                 : u.S - 1),
+                                 u.S - 1);
+            const int klo = kWindow ? max(0, u.off + qi - p.window_left) : 0;
 #ifdef TECOOPS_PREFILL_TRACE
             long long tr_busy = 0, tr_wait = 0, tr_prev = clock64(), tr_s = 0;
 #endif
             float m_s = -INFINITY;   // running max, scaled (log2) units
             float l = 0.f;
-            for (int j = 0; j < n; ++j) {
+            for (int j = u.J0; j < n; ++j) {
                 if (!__all_sync(0xffffffffu, mbar_wait_bounded(BAR(S_FULL + X), scount & 1,
                                                                abortp, p.dev_error, kSiteS))) {
                     ok = false;
                     break;
                 }
                 ++scount;
-                if (warp == 2 && lane == 0 && j == 0) UTRACE(ocount, 3, clock64());
+                if (warp == 2 && lane == 0 && j == u.J0) UTRACE(ocount, 3, clock64());
 #ifdef TECOOPS_PREFILL_TRACE
                 tr_s = clock64();
-                if (j > 0) tr_wait += tr_s - tr_prev;
+                if (j > u.J0) tr_wait += tr_s - tr_prev;
 #endif
                 tc_fence_after();
                 const int kbase = j * kBN;
-                // columns kbase + c >= kbase + nvalid are masked (causal / kv_len tail)
+                // columns c outside [nlo, nvalid) are masked (causal / window / kv_len tail)
                 const int nvalid = klim - kbase + 1;
-                const bool masked = __any_sync(0xffffffffu, nvalid < kBN);
+                const int nlo = kWindow ? klo - kbase : -kBN;
+                const bool masked = __any_sync(0xffffffffu, nvalid < kBN || (kWindow && nlo > 0));
                 // the whole 128-score row in registers: four loads, one wait
                 uint32_t uu[4][32];
 #pragma unroll
@@ -650,10 +675,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float mx = -INFINITY;
 #pragma unroll
                 for (int c = 0; c < kBN / 32; ++c)
-                    mx = masked ? chunk_max<true>(uu[c], nvalid - c * 32, mx)
-                                : chunk_max<false>(uu[c], 32, mx);
+                    mx = masked ? chunk_max<true>(uu[c], nlo - c * 32, nvalid - c * 32, mx)
+                                : chunk_max<false>(uu[c], 0, 32, mx);
                 const float m_new = fmaxf(m_s, mx * sl2);
-                const bool need = (j == 0) || (m_new > m_s + 8.0f);
+                const bool need = (j == u.J0) || (m_new > m_s + 8.0f);
                 const bool warp_need = __any_sync(0xffffffffu, need);
                 float alpha = 1.f;
                 if (warp_need) {
@@ -669,9 +694,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < kBN / 32; ++c) {
                     uint32_t pk[16];
                     if (masked)
-                        chunk_exp<T, true>(uu[c], nvalid - c * 32, sl2x2, negm2, sum2, pk);
+                        chunk_exp<T, true>(uu[c], nlo - c * 32, nvalid - c * 32, sl2x2, negm2,
+                                           sum2, pk);
                     else
-                        chunk_exp<T, false>(uu[c], 32, sl2x2, negm2, sum2, pk);
+                        chunk_exp<T, false>(uu[c], 0, 32, sl2x2, negm2, sum2, pk);
                     tmem_st16(tS + c * 16, pk);
                 }
                 float s0, s1, s2, s3;
@@ -679,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 f2unpack(sum2[1], s2, s3);
                 l = l * alpha + ((s0 + s1) + (s2 + s3));
                 // O rescale: PV_X(j-1) has completed (S_X(j), issued after it, has)
-                if (j > 0 && warp_need) {
+                if (j > u.J0 && warp_need) {
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
                         uint32_t v[32];
@@ -717,6 +743,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             const bool store = r < rows && qs + qi < p.total_q;
+            if (store && p.lse != nullptr)
+                p.lse[(int64_t)hx * p.total_q + qs + qi] =
+                    l > 0.f ? (m_s + log2f(l)) * 0.6931471805599453f : -INFINITY;
             T *orow = static_cast<T *>(p.out) + ((int64_t)(qs + qi) * p.num_heads + hx) * D;
             uint32_t ov[D / 32][32];
 #pragma unroll
@@ -859,9 +888,14 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, int num_
     p.total_q = s.total_q;
     p.batch = s.batch;
     p.scale_log2 = s.scale_log2;
+    p.causal = s.causal;
+    p.window_left = s.window_left;
+    p.window_right = s.window_right;
+    p.lse = s.lse;
     if (p.num_units <= 0 || s.batch <= 0) return cudaSuccess;
 
-    auto kfn = fa_prefill_sm100_kernel<T, D>;
+    auto kfn = s.window_left >= 0 ? fa_prefill_sm100_kernel<T, D, true>
+                                  : fa_prefill_sm100_kernel<T, D, false>;
     const int smem = PrefillSmem<D>::kAlloc;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;

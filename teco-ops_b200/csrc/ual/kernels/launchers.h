@@ -38,6 +38,13 @@ struct AttnShape {
     int max_q;
     int max_k;
     float scale_log2;         // softmax_scale * log2(e)
+    // key j is admissible for row i (off = kv_len - q_len) when j < kv_len and
+    //   j <= off + i (causal) or j <= off + i + window_right (non-causal, right >= 0)
+    //   j >= off + i - window_left (window_left >= 0)
+    int causal;
+    int window_left;
+    int window_right;
+    float *lse;               // optional [Hq, total_q] natural-log log-sum-exp
 };
 
 // ---- split-KV decode -------------------------------------------------------------
@@ -65,6 +72,8 @@ struct DecodeParams {
     float *part_o;      // [batch, Hq, max_splits, D]
     float *part_lse;    // [batch, Hq, max_splits]
     int *dev_error;     // error word for bounded waits (may be null)
+    int window_left;    // < 0: unbounded; else keys j >= kv_len - 1 - window_left
+    float *lse;         // optional [Hq, total_q] natural-log log-sum-exp
 };
 
 bool decode_supported(int head_dim, int block_size, int group);

@@ -33,6 +33,10 @@ static kern::AttnShape toShape(const FlashAttentionArgs &a) {
     s.max_q = a.max_q_seq_len;
     s.max_k = a.max_k_seq_len;
     s.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    s.causal = a.causal;
+    s.window_left = a.window_left;
+    s.window_right = a.window_right;
+    s.lse = a.softmax_lse;
     return s;
 }
 
@@ -65,6 +69,8 @@ static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
     p.part_o = nullptr;
     p.part_lse = nullptr;
     p.dev_error = a.dev_error;
+    p.window_left = a.window_left;   // q_len 1: causal and the right side change nothing
+    p.lse = a.softmax_lse;
     if (p.max_splits > 1) {
         const size_t need = kern::decode_workspace_bytes(p.batch, p.num_heads, p.head_dim,
                                                          p.max_splits);

@@ -28,13 +28,19 @@ EXPORTED = [
     "tecoopsGetTensor4dDescriptor", "tecoopsSetTensorNdDescriptor",
     "tecoopsGetTensorNdDescriptor", "tecoopsDestroyTensorDescriptor", "tecoopsMemset",
     "tecoopsReshapeAndCache", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
-    "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlattenRays", "tecoopsReduceVariance",
+    "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlashAttentionEx", "tecoopsFlattenRays", "tecoopsReduceVariance",
     "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsCausalConv1d",
 ]
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _lib = None
+
+
+class FlashAttentionOptions(ctypes.Structure):
+    """tecoopsFlashAttentionOptions_t."""
+    _fields_ = [("softmax_scale", ctypes.c_float), ("causal", _i), ("window_left", _i),
+                ("window_right", _i)]
 
 
 class TecoopsError(RuntimeError):
@@ -72,6 +78,9 @@ def lib():
         "tecoopsGetDeviceErrorStatus": [_vp, ctypes.POINTER(_i)],
         "tecoopsFlashAttentionDecodeNoAlloc": [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                                _vp, _vp, _vp, _vp],
+        "tecoopsFlashAttentionEx": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                    _vp, _vp, _vp, _vp, _vp,
+                                    ctypes.POINTER(FlashAttentionOptions), _vp],
         "tecoopsRmsNorm": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float],
     }
     for name, args in sig.items():
@@ -150,6 +159,23 @@ def flash_attention(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num, q
                                        _vp(block_table), q_desc.d, _vp(q), k_desc.d,
                                        _vp(k_cache), v_desc.d, _vp(v_cache), o_desc.d, _vp(out),
                                        _vp(workspace) if workspace else None)
+
+
+def flash_attention_ex(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num, q_seq_lens,
+                       kv_seq_lens, bt_desc: Desc, block_table, q_desc: Desc, q, k_desc: Desc,
+                       k_cache, v_desc: Desc, v_cache, o_desc: Desc, out, workspace=0,
+                       softmax_scale=0.0, causal=True, window=(-1, -1), softmax_lse=0) -> int:
+    """tecoopsFlashAttentionEx: scale (<= 0: 1/sqrt(D)), causal, window (left, right;
+    negative = unbounded) and an optional fp32 [Hq, total_q] log-sum-exp output."""
+    opts = FlashAttentionOptions(float(softmax_scale), 1 if causal else 0, int(window[0]),
+                                 int(window[1]))
+    return lib().tecoopsFlashAttentionEx(handle.h, max_seqlen_q, max_seqlen_k, max_block_num,
+                                         _vp(q_seq_lens), _vp(kv_seq_lens), bt_desc.d,
+                                         _vp(block_table), q_desc.d, _vp(q), k_desc.d,
+                                         _vp(k_cache), v_desc.d, _vp(v_cache), o_desc.d,
+                                         _vp(out), _vp(workspace) if workspace else None,
+                                         ctypes.byref(opts),
+                                         _vp(softmax_lse) if softmax_lse else None)
 
 
 def flash_attention_decode_noalloc(handle: Handle, max_seqlen_k, q_seq_lens, kv_seq_lens,

@@ -84,9 +84,12 @@ def reshape_inputs(c):
 
 
 # ---------------------------------------------------------------- flash_attention
-def _fa(q_lens, kv_lens, Hq, Hkv, D, bs, NB, dtype, dist, seed, bt="perm"):
-    return dict(q_lens=list(q_lens), kv_lens=list(kv_lens), Hq=Hq, Hkv=Hkv, D=D, bs=bs, NB=NB,
-                dtype=dtype, dist=dist, seed=seed, bt=bt)
+def _fa(q_lens, kv_lens, Hq, Hkv, D, bs, NB, dtype, dist, seed, bt="perm", opts=None):
+    c = dict(q_lens=list(q_lens), kv_lens=list(kv_lens), Hq=Hq, Hkv=Hkv, D=D, bs=bs, NB=NB,
+             dtype=dtype, dist=dist, seed=seed, bt=bt)
+    if opts:
+        c["opts"] = dict(opts)
+    return c
 
 
 ATTN_CASES = {
@@ -125,7 +128,49 @@ ATTN_CASES = {
                                    "normal", 44),
     "f16_generic_d96": _fa([33, 1], [40, 77], 6, 3, 96, 16, 16, "f16", "normal", 45),
     "bf16_generic_bs4": _fa([9], [23], 4, 2, 128, 4, 16, "bf16", "normal", 46),
+    # options of tecoopsFlashAttentionEx (the binding's softmax_scale / causal /
+    # window_size / return_softmax_lse).  "scale" and "causal" are pinned by the
+    # reference golden's own arguments; "window" and "lse" have no reference
+    # implementation (restated in the oracle, no golden fixture).
+    "opt_noncausal_prefill_bf16": _fa([200, 37, 513], [200, 300, 513], 32, 8, 128, 16, 160,
+                                      "bf16", "normal", 50, opts=dict(causal=False)),
+    "opt_noncausal_generic_f16": _fa([65], [90], 16, 2, 128, 8, 40, "f16", "normal", 51,
+                                     opts=dict(causal=False)),
+    "opt_scale_prefill_bf16_d64": _fa([130, 7], [130, 300], 16, 4, 64, 64, 16, "bf16", "normal",
+                                      52, opts=dict(scale=0.05)),
+    "opt_scale_decode_bf16": _fa([1] * 4, [17, 300, 1000, 2047], 32, 8, 128, 16, 400, "bf16",
+                                 "normal", 53, opts=dict(scale=0.3)),
+    "opt_window_prefill_bf16": _fa([300, 129, 520], [300, 400, 520], 32, 8, 128, 16, 160, "bf16",
+                                   "normal", 54, opts=dict(window=(100, 0))),
+    "opt_window_rowpairs_f16": _fa([700], [900], 6, 2, 128, 16, 64, "f16", "normal", 55,
+                                   opts=dict(window=(250, -1))),
+    "opt_window_noncausal_bf16": _fa([256, 64], [256, 200], 8, 2, 128, 16, 64, "bf16", "normal",
+                                     56, opts=dict(causal=False, window=(40, 24))),
+    "opt_window_decode_bf16": _fa([1] * 5, [1, 17, 300, 1000, 2047], 32, 8, 128, 16, 400, "bf16",
+                                  "normal", 57, opts=dict(window=(100, -1))),
+    "opt_window700_decode_f16": _fa([1] * 3, [2047, 701, 1500], 8, 1, 128, 32, 200, "f16",
+                                    "normal", 58, opts=dict(window=(700, -1))),
+    "opt_lse_prefill_bf16": _fa([200, 37, 513], [200, 300, 513], 32, 8, 128, 16, 160, "bf16",
+                                "normal", 59, opts=dict(lse=True)),
+    "opt_lse_decode_bf16": _fa([1] * 7, [1, 17, 300, 1000, 64, 5, 2047], 32, 8, 128, 16, 400,
+                               "bf16", "normal", 60, opts=dict(lse=True)),
+    "opt_lse_window_generic_f16": _fa([33, 1], [40, 77], 6, 3, 96, 16, 16, "f16", "normal", 61,
+                                      opts=dict(lse=True, window=(10, -1))),
+    "opt_all_prefill_f16_d64": _fa([130, 7], [130, 300], 16, 4, 64, 64, 16, "f16", "normal", 62,
+                                   opts=dict(scale=0.1, causal=False, window=(50, 20), lse=True)),
 }
+
+
+def attn_opts(c):
+    """Oracle keyword arguments of a case's options."""
+    o = c.get("opts", {})
+    return dict(softmax_scale=o.get("scale"), causal=o.get("causal", True),
+                window=tuple(o.get("window", (-1, -1))))
+
+
+def has_reference_golden(c):
+    """The reference golden covers scale and causal but no window."""
+    return "window" not in c.get("opts", {})
 
 
 def attn_inputs(c):

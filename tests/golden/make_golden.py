@@ -15,6 +15,9 @@ Goldens imported (three unavailable modules are stubbed in sys.modules):
   python_api_test/test_reshape_and_cache.py on the vLLM-layout view, as that
   test does (sdaa_to_cpu permute).
 
+Cases with options pass their softmax_scale / causal to both goldens; cases
+with a window are skipped (the reference has no windowed attention).
+
 Each fixture stores the case name, a deterministic sample of golden output
 values (float32) with their flat indices, float64 sum / abs-sum checksums, and
 for reshape the SHA-256 of the resulting caches in the SDAA layout.
@@ -83,9 +86,13 @@ def main(ref):
         bt = torch.from_numpy(inp["block_table"])
         ql = inp["q_lens"].tolist()
         kl = inp["kv_lens"].tolist()
-        g = zoo_golden(q, k, v, ql, kl, bt, causal=True,
-                       softmax_scale=1.0 / np.sqrt(float(c["D"]))).numpy()
-        g2 = api_golden(q, k, v, torch.tensor(ql), torch.tensor(kl), bt, causal=True).numpy()
+        if not cases.has_reference_golden(c):
+            continue   # windowed attention: no reference implementation
+        opts = cases.attn_opts(c)
+        scale = opts["softmax_scale"] or 1.0 / np.sqrt(float(c["D"]))
+        g = zoo_golden(q, k, v, ql, kl, bt, causal=opts["causal"], softmax_scale=scale).numpy()
+        g2 = api_golden(q, k, v, torch.tensor(ql), torch.tensor(kl), bt, causal=opts["causal"],
+                        softmax_scale=scale).numpy()
         assert np.array_equal(g, g2), f"reference goldens disagree on {name}"
         flat = g.reshape(-1).astype(np.float32)
         idx = cases.sample_index(flat.size)

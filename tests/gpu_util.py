@@ -61,6 +61,29 @@ def attention_capi(q, kc, vc, q_lens, kv_lens, bt, max_q=None, max_k=None, out=N
     return out
 
 
+def attention_ex_capi(q, kc, vc, q_lens, kv_lens, bt, opts, max_q=None, max_k=None):
+    """tecoopsFlashAttentionEx with a case's options dict (scale, causal, window, lse);
+    returns (out, lse or None)."""
+    dt = capi.DATA_HALF if q.dtype == torch.float16 else capi.DATA_BFLOAT16
+    out = torch.zeros_like(q)
+    lse = torch.full((q.shape[1], q.shape[0]), float("nan"), device=q.device) \
+        if opts.get("lse") else None
+    max_q = int(q_lens.max().item()) if max_q is None else max_q
+    max_k = int(kv_lens.max().item()) if max_k is None else max_k
+    descs = (capi.Desc(capi.DATA_INT32, bt.shape), capi.Desc(dt, q.shape),
+             capi.Desc(dt, kc.shape), capi.Desc(dt, vc.shape), capi.Desc(dt, out.shape))
+    st = capi.flash_attention_ex(handle(), max_q, max_k, kc.shape[0], q_lens.data_ptr(),
+                                 kv_lens.data_ptr(), descs[0], bt.data_ptr(), descs[1],
+                                 q.data_ptr(), descs[2], kc.data_ptr(), descs[3], vc.data_ptr(),
+                                 descs[4], out.data_ptr(), 0,
+                                 softmax_scale=opts.get("scale") or 0.0,
+                                 causal=opts.get("causal", True),
+                                 window=tuple(opts.get("window", (-1, -1))),
+                                 softmax_lse=lse.data_ptr() if lse is not None else 0)
+    capi.check(st, "tecoopsFlashAttentionEx")
+    return out, lse
+
+
 def attn_case_to_dev(inp, dtype):
     return dict(q=words_to_dev(inp["q"], dtype), kc=words_to_dev(inp["k_cache"], dtype),
                 vc=words_to_dev(inp["v_cache"], dtype),

@@ -14,6 +14,7 @@ pytestmark = pytest.mark.gpu
 MAX_ABS = 2e-2
 MEAN_ABS = 2e-3
 DIFF1 = 1e-2
+LSE_ABS = 2e-3   # log-sum-exp (natural log) of the options cases
 
 
 @pytest.fixture(autouse=True)
@@ -22,27 +23,41 @@ def _need_cuda():
         pytest.skip("no CUDA device")
 
 
-def _run_case(c):
-    from gpu_util import attention_capi, attn_case_to_dev
+def _run_case(c, with_lse=False):
+    from gpu_util import attention_capi, attention_ex_capi, attn_case_to_dev
     inp = cases.attn_inputs(c)
     d = attn_case_to_dev(inp, c["dtype"])
-    out = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"])
+    lse = None
+    if "opts" in c:
+        out, lse = attention_ex_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"],
+                                     c["opts"])
+    else:
+        out = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"])
     torch.cuda.synchronize()
-    return inp, out.float().cpu().numpy()
+    out = out.float().cpu().numpy()
+    if with_lse:
+        return inp, out, (lse.cpu().numpy() if lse is not None else None)
+    return inp, out
 
 
 @pytest.mark.parametrize("name", sorted(cases.ATTN_CASES))
 def test_attention_vs_oracle_and_golden(golden, name):
     from gpu_util import errors
     c = cases.ATTN_CASES[name]
-    inp, out = _run_case(c)
-    ref = oracle.flash_attn_varlen(
+    inp, out, lse = _run_case(c, with_lse=True)
+    ref, rlse = oracle.flash_attn_varlen(
         seeded.words_to_f32(inp["q"], c["dtype"]), seeded.words_to_f32(inp["k_cache"], c["dtype"]),
         seeded.words_to_f32(inp["v_cache"], c["dtype"]), inp["q_lens"], inp["kv_lens"],
-        inp["block_table"])
+        inp["block_table"], return_lse=True, **cases.attn_opts(c))
     assert np.isfinite(out).all()
     mx, mean, diff1 = errors(out, ref)
     assert mx <= MAX_ABS and mean <= MEAN_ABS and diff1 <= DIFF1, (mx, mean, diff1)
+    if lse is not None:
+        fin = np.isfinite(rlse)
+        assert np.array_equal(np.isfinite(lse), fin) and not np.isnan(lse).any()
+        assert np.abs(lse[fin] - rlse[fin]).max() <= LSE_ABS, np.abs(lse[fin] - rlse[fin]).max()
+    if not cases.has_reference_golden(c):
+        return   # windowed: the oracle is the only reference
     idx = golden[f"attn/{name}/idx"]
     gmx, gmean, _ = errors(out.reshape(-1)[idx], golden[f"attn/{name}/val"])
     assert gmx <= MAX_ABS and gmean <= MEAN_ABS, (gmx, gmean)

@@ -20,11 +20,13 @@ def test_fixture_meta_matches_cases(golden):
 @pytest.mark.parametrize("name", sorted(cases.ATTN_CASES))
 def test_attention_oracle_vs_reference_golden(golden, name):
     c = cases.ATTN_CASES[name]
+    if not cases.has_reference_golden(c):
+        pytest.skip("windowed attention has no reference golden")
     inp = cases.attn_inputs(c)
     out = oracle.flash_attn_varlen(
         seeded.words_to_f32(inp["q"], c["dtype"]), seeded.words_to_f32(inp["k_cache"], c["dtype"]),
         seeded.words_to_f32(inp["v_cache"], c["dtype"]), inp["q_lens"], inp["kv_lens"],
-        inp["block_table"])
+        inp["block_table"], **cases.attn_opts(c))
     flat = out.reshape(-1)
     idx = golden[f"attn/{name}/idx"]
     # numpy vs torch fp32 BLAS: only accumulation-order differences
@@ -64,3 +66,74 @@ def test_flop_and_byte_counts():
     assert oracle.attention.causal_pairs([2], [5]) == 4 + 5
     assert oracle.attention_flops([256], [256], 8, 128) == 4 * 128 * 8 * 256 * 257 // 2
     assert oracle.reshape_bytes(np.array([0, -1, 3]), 8, 128) == 8 * 3 + 4 * 2 * 8 * 128 * 2
+
+
+def _small_case(seed=5, L=(40, 9), S=(70, 9), Hq=4, Hkv=2, D=16, bs=8):
+    rng = np.random.default_rng(seed)
+    NB = sum((s + bs - 1) // bs for s in S)
+    q = rng.standard_normal((sum(L), Hq, D)).astype(np.float32)
+    kc = rng.standard_normal((NB, Hkv, bs, D)).astype(np.float32)
+    vc = rng.standard_normal((NB, Hkv, bs, D)).astype(np.float32)
+    bt = np.zeros((len(L), max((s + bs - 1) // bs for s in S)), np.int32)
+    p = 0
+    for b, s in enumerate(S):
+        n = (s + bs - 1) // bs
+        bt[b, :n] = np.arange(p, p + n)
+        p += n
+    return q, kc, vc, list(L), list(S), bt
+
+
+def _brute(q, kc, vc, L, S, bt, scale, causal, window):
+    """Per (row, head) loop: explicit admissible key set, softmax, log-sum-exp."""
+    Hq, D = q.shape[1], q.shape[2]
+    Hkv, bs = kc.shape[1], kc.shape[2]
+    out = np.zeros_like(q, dtype=np.float64)
+    lse = np.full((Hq, q.shape[0]), -np.inf)
+    r0 = 0
+    for b in range(len(L)):
+        off = S[b] - L[b]
+        for i in range(L[b]):
+            for h in range(Hq):
+                kv = h // (Hq // Hkv)
+                keys = []
+                for j in range(S[b]):
+                    hi = off + i if causal else (off + i + window[1] if window[1] >= 0 else 1 << 30)
+                    lo = off + i - window[0] if window[0] >= 0 else -(1 << 30)
+                    if lo <= j <= hi:
+                        keys.append(j)
+                if not keys:
+                    continue
+                ks = np.array([kc[bt[b, j // bs], kv, j % bs] for j in keys], np.float64)
+                vs = np.array([vc[bt[b, j // bs], kv, j % bs] for j in keys], np.float64)
+                x = ks @ q[r0 + i, h].astype(np.float64) * scale
+                m = x.max()
+                w = np.exp(x - m)
+                out[r0 + i, h] = w @ vs / w.sum()
+                lse[h, r0 + i] = m + np.log(w.sum())
+        r0 += L[b]
+    return out, lse
+
+
+@pytest.mark.parametrize("causal,window", [(True, (-1, -1)), (False, (-1, -1)), (True, (7, -1)),
+                                           (False, (5, 3)), (False, (-1, 0)), (True, (0, -1))])
+def test_oracle_options_vs_brute_force(causal, window):
+    """Window and log-sum-exp (no reference implementation) against a direct
+    per-row restatement of their definitions."""
+    q, kc, vc, L, S, bt = _small_case()
+    out, lse = oracle.flash_attn_varlen(q, kc, vc, L, S, bt, softmax_scale=0.3, causal=causal,
+                                        window=window, return_lse=True)
+    ref, rlse = _brute(q, kc, vc, L, S, bt, 0.3, causal, window)
+    np.testing.assert_allclose(out, ref, atol=2e-5)
+    fin = np.isfinite(rlse)
+    assert np.array_equal(fin, np.isfinite(lse))
+    np.testing.assert_allclose(lse[fin], rlse[fin], atol=2e-5)
+
+
+def test_oracle_window_properties():
+    q, kc, vc, L, S, bt = _small_case(seed=6)
+    base = oracle.flash_attn_varlen(q, kc, vc, L, S, bt)
+    # a window wider than every sequence changes nothing; non-causal with right 0 is causal
+    np.testing.assert_array_equal(
+        oracle.flash_attn_varlen(q, kc, vc, L, S, bt, window=(10_000, -1)), base)
+    np.testing.assert_array_equal(
+        oracle.flash_attn_varlen(q, kc, vc, L, S, bt, causal=False, window=(-1, 0)), base)

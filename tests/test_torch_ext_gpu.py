@@ -59,6 +59,40 @@ def test_flash_attn_varlen_func_reference_signature(name):
     assert mx <= 2e-2 and mean <= 2e-3
 
 
+@pytest.mark.parametrize("name", ["opt_window_noncausal_bf16", "opt_lse_decode_bf16",
+                                  "opt_all_prefill_f16_d64", "opt_scale_prefill_bf16_d64"])
+def test_flash_attn_varlen_func_honours_flags(name):
+    """softmax_scale / causal / window_size / return_softmax_lse reach the kernels
+    (the reference binding ignores them)."""
+    import tecoops
+    from gpu_util import attention_ex_capi, attn_case_to_dev, errors
+    c = cases.ATTN_CASES[name]
+    o = c["opts"]
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    ql = inp["q_lens"]
+    cu = torch.zeros(len(ql) + 1, dtype=torch.int32)
+    cu[1:] = torch.from_numpy(np.cumsum(ql)).to(torch.int32)
+    win = torch.tensor(o["window"], dtype=torch.int32) if "window" in o else torch.Tensor()
+    res = tecoops.flash_attn_varlen_func(
+        d["q"], d["kc"], d["vc"], int(ql.max()), cu.cuda(), int(inp["kv_lens"].max()),
+        torch.Tensor(), d["kv_lens"], float(o.get("scale") or 0.0), bool(o.get("causal", True)),
+        win, d["bt"], bool(o.get("lse", False)), torch.empty_like(d["q"]))
+    out, lse = res if o.get("lse") else (res, None)
+    ref_out, ref_lse = attention_ex_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"],
+                                         d["bt"], o)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out)
+    if lse is not None:
+        assert torch.equal(lse, ref_lse)
+    ref = oracle.flash_attn_varlen(
+        seeded.words_to_f32(inp["q"], c["dtype"]), seeded.words_to_f32(inp["k_cache"], c["dtype"]),
+        seeded.words_to_f32(inp["v_cache"], c["dtype"]), inp["q_lens"], inp["kv_lens"],
+        inp["block_table"], **cases.attn_opts(c))
+    mx, mean, _ = errors(out.float().cpu().numpy(), ref)
+    assert mx <= 2e-2 and mean <= 2e-3
+
+
 def test_torch_library_ops():
     import tecoops  # noqa: F401  (registers torch.ops.tecoops)
     from gpu_util import attention_capi, attn_case_to_dev

@@ -262,6 +262,17 @@ class Workloads:
                                        self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr())
         self.capi.check(st, "flash_attention")
 
+    def decode_fused(self):
+        """The same step through tecoopsReshapeAndCacheFlashAttentionDecode (one launch
+        for the scatter and the split-KV pass, plus the split merge)."""
+        bt_d, q_d, c_d = self.d_desc
+        st = self.capi.reshape_and_cache_flash_attention_decode(
+            self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(), self.d_slot.data_ptr(),
+            self.d_maxk, self.d_ones.data_ptr(), self.d_ctx.data_ptr(), bt_d,
+            self.d_bt3.data_ptr(), q_d, self.d_q3.data_ptr(), c_d, self.d_kc.data_ptr(), c_d,
+            self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr())
+        self.capi.check(st, "reshape_and_cache_flash_attention_decode")
+
     # ---- config 4: reshape sweep point (T = 65536, scattered, no padding)
     def setup_reshape(self, rank: int):
         torch = self.torch
@@ -361,6 +372,8 @@ def run_ours(args):
     dec_ms = max_over_ranks(sum(a + b for a, b in zip(tr, ta)))
     dec_attn_avg = sum(ta) / len(ta)
     dec_bytes_step = W.decode_bytes + W.decode_reshape_bytes
+    (tf,) = timed_loop(torch, args.steps, args.warmup, [W.decode_fused])
+    dec_fused_ms = max_over_ranks(sum(tf))
     decode = {
         "workload": "config 3: B=64 paged decode, ctx U{512..8192}+1, 40k-page pool, bs 16, bf16",
         "metric": "decode HBM GB/s", "unit": "GB/s",
@@ -370,6 +383,10 @@ def run_ours(args):
         "attn_gbs": W.decode_bytes / (dec_attn_avg * 1e-3) / 1e9,
         "attn_frac_of_measured_hbm": W.decode_bytes / (dec_attn_avg * 1e-3) / 1e9 / peaks["hbm_gbs"],
         "l2": "inputs (1.1 GB of K/V) larger than L2",
+        "fused": {"api": "tecoopsReshapeAndCacheFlashAttentionDecode (scatter + attention in "
+                         "one launch, same bytes)",
+                  "ms_per_step": dec_fused_ms / args.steps,
+                  "value": world * args.steps * dec_bytes_step / (dec_fused_ms * 1e-3) / 1e9},
     }
     del W.d_kc, W.d_vc
     torch.cuda.empty_cache()

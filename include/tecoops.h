@@ -210,6 +210,27 @@ tecoopsStatus_t tecoopsFlashAttentionEx(tecoopsHandle_t handle,
                                         float *softmax_lse);
 
 /*
+ * Extension: one decode step's tecoopsReshapeAndCache + tecoopsFlashAttention in
+ * one launch (reference reshape_and_cache_fp16.scpp:47-96 followed by
+ * flash_attention.scpp:237-245 with q_len 1).  Every sequence has q_len 0 or 1;
+ * row t of key/value ([sum(q_len), num_kv_heads, head_size], the cache dtype) is
+ * the new token of the sequence whose query is row t, stored at cache slot
+ * slot_mapping[t] (int64, -1 = skip) and attended at position kv_len - 1
+ * (kv_seq_lens count the new token).  Results equal tecoopsReshapeAndCache
+ * followed by tecoopsFlashAttention(max_seqlen_q = 1) when slot_mapping[t] is
+ * the slot of position kv_len - 1 in the block table.  Shapes outside the
+ * split-KV kernel run the two operators back to back.
+ */
+tecoopsStatus_t tecoopsReshapeAndCacheFlashAttentionDecode(
+    tecoopsHandle_t handle, const void *key, const void *value, const int64_t *slot_mapping,
+    int max_seqlen_k, const int *q_seq_lens, const int *kv_seq_lens,
+    const tecoopsTensorDescriptor_t blockTableDesc, const void *blockTable,
+    const tecoopsTensorDescriptor_t qDataDesc, const void *qData,
+    const tecoopsTensorDescriptor_t kCacheDesc, void *kCache,
+    const tecoopsTensorDescriptor_t vCacheDesc, void *vCache,
+    const tecoopsTensorDescriptor_t oDataDesc, void *oData, void *workspace);
+
+/*
  * Extension (no counterpart in the reference, whose `workspace` is always
  * nullptr): bytes of device scratch tecoopsFlashAttention needs for these
  * shapes, so that a caller can pass its own `workspace`.

@@ -96,6 +96,9 @@ static void fillArgs(FlashAttentionArgs &a, tecoopsHandle_t handle, int max_seql
     a.window_left = -1;
     a.window_right = -1;
     a.softmax_lse = nullptr;
+    a.new_key = nullptr;
+    a.new_value = nullptr;
+    a.slot_mapping = nullptr;
 }
 
 extern "C" tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(
@@ -174,6 +177,63 @@ extern "C" tecoopsStatus_t tecoopsFlashAttention(
     return flashAttentionImpl(handle, max_seqlen_q, max_seqlen_k, q_seq_lens, kv_seq_lens,
                               blockTableDesc, blockTable, qDataDesc, qData, kCacheDesc, kCache,
                               vCacheDesc, vCache, oDataDesc, oData, workspace, nullptr, nullptr);
+}
+
+extern "C" tecoopsStatus_t tecoopsReshapeAndCacheFlashAttentionDecode(
+    tecoopsHandle_t handle, const void *key, const void *value, const int64_t *slot_mapping,
+    int max_seqlen_k, const int *q_seq_lens, const int *kv_seq_lens,
+    const tecoopsTensorDescriptor_t blockTableDesc, const void *blockTable,
+    const tecoopsTensorDescriptor_t qDataDesc, const void *qData,
+    const tecoopsTensorDescriptor_t kCacheDesc, void *kCache,
+    const tecoopsTensorDescriptor_t vCacheDesc, void *vCache,
+    const tecoopsTensorDescriptor_t oDataDesc, void *oData, void *workspace) {
+    tecoopsStatus_t st = flashAttentionCheckArgs(handle, blockTableDesc, qDataDesc, kCacheDesc,
+                                                 vCacheDesc, oDataDesc);
+    if (st != TECOOPS_STATUS_SUCCESS) return st;
+    if (!key || !value || !slot_mapping || !q_seq_lens || !kv_seq_lens || !blockTable ||
+        !kCache || !vCache || max_seqlen_k < 0)
+        return TECOOPS_STATUS_BAD_PARAM;
+    const int T = qDataDesc->dimA[0];
+    if (T == 0) return TECOOPS_STATUS_SUCCESS;
+    if (!qData || !oData) return TECOOPS_STATUS_BAD_PARAM;
+    FlashAttentionArgs args{};
+    fillArgs(args, handle, 1, max_seqlen_k, blockTableDesc, qDataDesc, kCacheDesc);
+    if (FlashAttentionOp::selectAlgo(args) !=
+            tecoops::ual::ops::FlashAttentionAlgos::DECODE_SPLITKV ||
+        (args.size_per_head % 8) != 0) {
+        // shapes outside the split-KV kernel: the two operators back to back
+        st = tecoopsReshapeAndCache(handle, key, value, slot_mapping, kCache, vCache, T,
+                                    args.local_kv_head_num, args.size_per_head,
+                                    args.max_block_num, args.block_size);
+        if (st != TECOOPS_STATUS_SUCCESS) return st;
+        return flashAttentionImpl(handle, 1, max_seqlen_k, q_seq_lens, kv_seq_lens,
+                                  blockTableDesc, blockTable, qDataDesc, qData, kCacheDesc,
+                                  kCache, vCacheDesc, vCache, oDataDesc, oData, workspace,
+                                  nullptr, nullptr);
+    }
+    args.q_seq_lens = q_seq_lens;
+    args.kv_seq_lens = kv_seq_lens;
+    args.block_table = static_cast<const int *>(blockTable);
+    args.q = qData;
+    args.key_cache = kCache;
+    args.value_cache = vCache;
+    args.fmha_out = oData;
+    args.new_key = key;
+    args.new_value = value;
+    args.slot_mapping = slot_mapping;
+    const size_t need = FlashAttentionOp::workspaceSize(args);
+    if (workspace != nullptr) {
+        args.workspace = workspace;
+        args.workspace_bytes = need;
+    } else if (need > 0) {
+        args.workspace = tecoops::interface::handleScratch(handle, need);
+        if (args.workspace == nullptr) return TECOOPS_STATUS_ALLOC_FAILED;
+        args.workspace_bytes = handle->scratch_bytes;
+    }
+    args.dev_error = tecoops::interface::handleErrorWord(handle);
+    FlashAttentionPatchArgs patch{&args};
+    TECOOPS_RUN_OP(FlashAttentionOp, args, patch, handle);
+    return TECOOPS_STATUS_SUCCESS;
 }
 
 extern "C" tecoopsStatus_t tecoopsFlashAttentionEx(

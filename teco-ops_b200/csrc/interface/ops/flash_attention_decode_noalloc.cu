@@ -141,6 +141,9 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
     p.dev_error = nullptr;
     p.window_left = -1;
     p.lse = nullptr;
+    p.new_key = nullptr;
+    p.new_value = nullptr;
+    p.slot_mapping = nullptr;
     const size_t need =
         tecoops::kern::decode_workspace_bytes(batch, heads, head_dim, p.max_splits);
     if (need > kNoAllocScratchBytes) {

@@ -44,6 +44,10 @@ struct FlashAttentionArgs {
     int window_left;         // < 0: unbounded
     int window_right;        // < 0: unbounded (ignored when causal)
     float *softmax_lse;      // optional fp32 [Hq, total_q], natural log
+    // fused reshape_and_cache of each sequence's new token (decode branch only)
+    const void *new_key;     // [total_q, Hkv, D] or null
+    const void *new_value;
+    const int64_t *slot_mapping;
 };
 
 // Branch selection input (reference FlashAttentionPatchArgs).

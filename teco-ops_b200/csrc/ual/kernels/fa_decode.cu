@@ -28,6 +28,12 @@
 //  * options: a left window (keys j >= kv_len - 1 - window_left) moves the first
 //    split to the window's 16-token chunk and masks the keys before it; the
 //    log-sum-exp (natural log) of each row is written when requested.
+//  * fused reshape_and_cache (tecoopsReshapeAndCacheFlashAttentionDecode): the CTA of a
+//    sequence's last split (Q slice 0) stores the new token's K/V row of its KV head
+//    into the cache slot, and the consumer warp whose chunk holds position kv_len - 1
+//    overwrites that row of the staged K/V tiles from the new key/value, so the
+//    attention never depends on the ordering of the store and the TMA read of the
+//    same slot; one launch replaces the scatter kernel + decode.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -98,6 +104,21 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int kv_end = min(kv_len, kv_begin + p.split_tokens);
     const int qrow = warp_seq_start(p.q_seq_lens, b);   // q_len == 1 on this path
     if (qrow >= p.total_q) return;                      // lengths beyond q's rows
+    const bool fused = p.new_key != nullptr;
+    if (fused && slice == 0 && split == max(n_split_b, 1) - 1 && tid < D / 8) {
+        // reshape_and_cache of the new token, this KV head: one 16-byte chunk per thread
+        const int64_t slot = __ldg(p.slot_mapping + qrow);
+        if (slot >= 0 && slot < (int64_t)p.num_pages * p.block_size) {
+            const int64_t page = slot / p.block_size;
+            const int64_t dst =
+                ((page * p.num_kv_heads + kvh) * p.block_size + (slot - page * p.block_size)) * D;
+            const int64_t src = ((int64_t)qrow * p.num_kv_heads + kvh) * D;
+            reinterpret_cast<uint4 *>(const_cast<void *>(p.key_cache))[(dst >> 3) + tid] =
+                __ldg(reinterpret_cast<const uint4 *>(p.new_key) + (src >> 3) + tid);
+            reinterpret_cast<uint4 *>(const_cast<void *>(p.value_cache))[(dst >> 3) + tid] =
+                __ldg(reinterpret_cast<const uint4 *>(p.new_value) + (src >> 3) + tid);
+        }
+    }
     const int nch = kv_end > kv_begin ? (kv_end - kv_begin + kChunk - 1) / kChunk : 0;
 
     const int head0 = kvh * p.group + slice * 16;   // first q head of this tile
@@ -220,6 +241,21 @@ __global__ void __launch_bounds__(kThreads, 3)
                     const int r = nv + idx / (D / 8);
                     const int ch = idx % (D / 8);
                     *reinterpret_cast<uint4 *>(vt + swz128(r, ch)) = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async_smem();   // ordered before TMA refills this stage
+                __syncwarp();
+            }
+            const int rn = kv_len - 1 - tok0;   // row of the new token in this chunk
+            if (fused && rn >= 0 && rn < kChunk) {
+                // the new token's K and V come from the inputs, not from the cache
+                uint8_t *kt = sgen + (ktile - sbase);
+                uint8_t *vt = kt + Sm::kTileBytes;
+                const int64_t src = ((int64_t)qrow * p.num_kv_heads + kvh) * D;
+                for (int ch = lane; ch < D / 8; ch += 32) {
+                    *reinterpret_cast<uint4 *>(kt + swz128(rn, ch)) =
+                        __ldg(reinterpret_cast<const uint4 *>(p.new_key) + (src >> 3) + ch);
+                    *reinterpret_cast<uint4 *>(vt + swz128(rn, ch)) =
+                        __ldg(reinterpret_cast<const uint4 *>(p.new_value) + (src >> 3) + ch);
                 }
                 fence_proxy_async_smem();   // ordered before TMA refills this stage
                 __syncwarp();

@@ -74,6 +74,12 @@ struct DecodeParams {
     int *dev_error;     // error word for bounded waits (may be null)
     int window_left;    // < 0: unbounded; else keys j >= kv_len - 1 - window_left
     float *lse;         // optional [Hq, total_q] natural-log log-sum-exp
+    // fused reshape_and_cache (all null when unfused): the new token of sequence b is
+    // q row b's key/value [total_q, Hkv, D], written to cache slot slot_mapping[row]
+    // (skipped when < 0) and attended at position kv_len - 1 from these inputs
+    const void *new_key;
+    const void *new_value;
+    const int64_t *slot_mapping;
 };
 
 bool decode_supported(int head_dim, int block_size, int group);

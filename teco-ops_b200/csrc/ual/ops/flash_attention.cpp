@@ -71,6 +71,9 @@ static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
     p.dev_error = a.dev_error;
     p.window_left = a.window_left;   // q_len 1: causal and the right side change nothing
     p.lse = a.softmax_lse;
+    p.new_key = a.new_key;
+    p.new_value = a.new_value;
+    p.slot_mapping = a.slot_mapping;
     if (p.max_splits > 1) {
         const size_t need = kern::decode_workspace_bytes(p.batch, p.num_heads, p.head_dim,
                                                          p.max_splits);

@@ -28,7 +28,8 @@ EXPORTED = [
     "tecoopsGetTensor4dDescriptor", "tecoopsSetTensorNdDescriptor",
     "tecoopsGetTensorNdDescriptor", "tecoopsDestroyTensorDescriptor", "tecoopsMemset",
     "tecoopsReshapeAndCache", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
-    "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlashAttentionEx", "tecoopsFlattenRays", "tecoopsReduceVariance",
+    "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlashAttentionEx",
+    "tecoopsReshapeAndCacheFlashAttentionDecode", "tecoopsFlattenRays", "tecoopsReduceVariance",
     "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsCausalConv1d",
 ]
 
@@ -81,6 +82,9 @@ def lib():
         "tecoopsFlashAttentionEx": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _vp,
                                     ctypes.POINTER(FlashAttentionOptions), _vp],
+        "tecoopsReshapeAndCacheFlashAttentionDecode": [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp,
+                                                       _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                       _vp, _vp],
         "tecoopsRmsNorm": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float],
     }
     for name, args in sig.items():
@@ -176,6 +180,18 @@ def flash_attention_ex(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num
                                          _vp(out), _vp(workspace) if workspace else None,
                                          ctypes.byref(opts),
                                          _vp(softmax_lse) if softmax_lse else None)
+
+
+def reshape_and_cache_flash_attention_decode(handle: Handle, key, value, slot_mapping,
+                                             max_seqlen_k, q_seq_lens, kv_seq_lens,
+                                             bt_desc: Desc, block_table, q_desc: Desc, q,
+                                             k_desc: Desc, k_cache, v_desc: Desc, v_cache,
+                                             o_desc: Desc, out, workspace=0) -> int:
+    """One decode step: scatter of the new tokens' K/V and attention in one launch."""
+    return lib().tecoopsReshapeAndCacheFlashAttentionDecode(
+        handle.h, _vp(key), _vp(value), _vp(slot_mapping), max_seqlen_k, _vp(q_seq_lens),
+        _vp(kv_seq_lens), bt_desc.d, _vp(block_table), q_desc.d, _vp(q), k_desc.d, _vp(k_cache),
+        v_desc.d, _vp(v_cache), o_desc.d, _vp(out), _vp(workspace) if workspace else None)
 
 
 def flash_attention_decode_noalloc(handle: Handle, max_seqlen_k, q_seq_lens, kv_seq_lens,

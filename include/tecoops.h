@@ -84,7 +84,30 @@ typedef enum {
     TECOOPS_DATA_DOUBLE = 8,
     TECOOPS_DATA_BFLOAT16 = 9,
     TECOOPS_DATA_COMPLEX_FLOAT = 10,
+    /* extension: 8-bit float KV cache (e4m3, finite saturation) with a per-tensor scale */
+    TECOOPS_DATA_FLOAT8_E4M3 = 32,
 } tecoopsDataType_t;
+
+/* extension: page layouts of the paged K/V cache */
+typedef enum {
+    TECOOPS_KV_LAYOUT_HND = 0, /* [num_blocks, num_kv_heads, block_size, head_size] (reference) */
+    TECOOPS_KV_LAYOUT_NHD = 1, /* [num_blocks, block_size, num_kv_heads, head_size] (vLLM)      */
+} tecoopsKvLayout_t;
+
+/*
+ * extension: how a paged K/V cache is stored.
+ *   kv_layout    : tecoopsKvLayout_t
+ *   cache_dtype  : TECOOPS_DATA_HALF / TECOOPS_DATA_BFLOAT16 (the key's dtype; bit-exact
+ *                  copy) or TECOOPS_DATA_FLOAT8_E4M3 (cache = e4m3(x / scale), saturated
+ *                  to +-448; attention reads back e4m3 * scale)
+ *   k_scale, v_scale : per-tensor scales of an FP8 cache (<= 0 means 1)
+ */
+typedef struct tecoopsKvCacheConfig {
+    int kv_layout;
+    tecoopsDataType_t cache_dtype;
+    float k_scale;
+    float v_scale;
+} tecoopsKvCacheConfig_t;
 
 typedef struct tecoopsContext *tecoopsHandle_t;
 typedef struct tecoopsTensorStruct *tecoopsTensorDescriptor_t;
@@ -130,6 +153,19 @@ tecoopsStatus_t tecoopsMemset(tecoopsHandle_t handle, void *x, const int value, 
  * reference writes out of bounds there).  Two tokens mapped to the same slot
  * race, as in the reference.
  */
+/*
+ * Extension: reshape_and_cache into a cache described by `cache` (nullptr: the
+ * reference's layout and a bit-exact copy).  key_dtype is TECOOPS_DATA_HALF or
+ * TECOOPS_DATA_BFLOAT16; num_kv_heads / block_size keep their meaning whatever the
+ * layout.
+ */
+tecoopsStatus_t tecoopsReshapeAndCacheEx(tecoopsHandle_t handle, const void *key,
+                                         const void *value, const int64_t *slot_mapping,
+                                         void *key_cache, void *value_cache, int num_tokens,
+                                         int num_kv_heads, int head_size, int num_blocks,
+                                         int block_size, tecoopsDataType_t key_dtype,
+                                         const tecoopsKvCacheConfig_t *cache);
+
 tecoopsStatus_t tecoopsReshapeAndCache(tecoopsHandle_t handle,
                                        const void *key, const void *value,
                                        const int64_t *slot_mapping,
@@ -184,6 +220,11 @@ typedef struct tecoopsFlashAttentionOptions {
     int causal;
     int window_left;
     int window_right;
+    /* cache storage: layout (the cache descriptors' dims follow it) and, for a
+       TECOOPS_DATA_FLOAT8_E4M3 cache (descriptor dtype), the dequantisation scales */
+    int kv_layout;
+    float k_scale;
+    float v_scale;
 } tecoopsFlashAttentionOptions_t;
 
 /*

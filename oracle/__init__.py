@@ -9,6 +9,8 @@ package and ``libteco_ops.so``) never imports, links or calls anything here.
   test/zoo/teco/reshape_and_cache/reshape_and_cache.cpp:136-147.
 * :func:`flash_attn_varlen`: the torch golden
   test/zoo/teco/flash_attention/flash_attention.py:79-140 restated in numpy fp32.
+* :mod:`oracle.fp8`: e4m3 encode / decode of the FP8 KV-cache extension (OCP E4M3
+  definition; no reference counterpart).
 * :mod:`oracle.seeded`: deterministic counter-based input generator shared by
   the golden-fixture script and the parity tests.
 

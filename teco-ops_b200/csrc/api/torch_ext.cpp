@@ -146,7 +146,10 @@ pybind11::object flash_attn_varlen_func_torch(torch::Tensor q, torch::Tensor k, 
                                               torch::Tensor block_table, bool return_softmax_lse,
                                               torch::Tensor out) {
     (void)cu_seqlens_k;
-    tecoopsFlashAttentionOptions_t opts;
+    tecoopsFlashAttentionOptions_t opts{};
+    opts.kv_layout = TECOOPS_KV_LAYOUT_HND;
+    opts.k_scale = 1.f;
+    opts.v_scale = 1.f;
     opts.softmax_scale = softmax_scale > 0.0 ? (float)softmax_scale : 0.f;
     opts.causal = causal ? 1 : 0;
     opts.window_left = -1;

@@ -34,12 +34,19 @@ static bool packed(const tecoopsTensorStruct *d) {
     return true;
 }
 
+static bool is16(tecoopsDataType_t t) {
+    return t == TECOOPS_DATA_HALF || t == TECOOPS_DATA_BFLOAT16;
+}
+
+// layout: cache dims [NB, Hkv, bs, D] (0) or [NB, bs, Hkv, D] (1); allow_fp8: the
+// caches may be TECOOPS_DATA_FLOAT8_E4M3 (then q / out carry the 16-bit dtype)
 static tecoopsStatus_t flashAttentionCheckArgs(tecoopsHandle_t handle,
                                                const tecoopsTensorDescriptor_t bt,
                                                const tecoopsTensorDescriptor_t q,
                                                const tecoopsTensorDescriptor_t k,
                                                const tecoopsTensorDescriptor_t v,
-                                               const tecoopsTensorDescriptor_t o) {
+                                               const tecoopsTensorDescriptor_t o,
+                                               int layout = 0, bool allow_fp8 = false) {
     if (handle == nullptr) {
         TECO_ERROR("tecoopsHandle_t is nullptr");
         return TECOOPS_STATUS_NOT_INITIALIZED;
@@ -49,7 +56,8 @@ static tecoopsStatus_t flashAttentionCheckArgs(tecoopsHandle_t handle,
         TECO_ERROR("k_cache data_type must be equal to v_cache data_type");
         return TECOOPS_STATUS_BAD_PARAM;
     }
-    if (k->dataType != TECOOPS_DATA_HALF && k->dataType != TECOOPS_DATA_BFLOAT16) {
+    const bool fp8 = allow_fp8 && k->dataType == TECOOPS_DATA_FLOAT8_E4M3;
+    if (!is16(k->dataType) && !fp8) {
         TECO_ERROR("k/v cache must be TECOOPS_DATA_HALF or TECOOPS_DATA_BFLOAT16");
         return TECOOPS_STATUS_BAD_PARAM;
     }
@@ -61,7 +69,8 @@ static tecoopsStatus_t flashAttentionCheckArgs(tecoopsHandle_t handle,
             return TECOOPS_STATUS_BAD_PARAM;
         }
     }
-    if (q->dataType != k->dataType || o->dataType != k->dataType) return TECOOPS_STATUS_BAD_PARAM;
+    if (!is16(q->dataType) || o->dataType != q->dataType || (!fp8 && q->dataType != k->dataType))
+        return TECOOPS_STATUS_BAD_PARAM;
     for (int i = 0; i < 3; ++i)
         if (q->dimA[i] != o->dimA[i]) return TECOOPS_STATUS_BAD_PARAM;
     if (bt->dataType != TECOOPS_DATA_INT32) return TECOOPS_STATUS_BAD_PARAM;
@@ -69,7 +78,8 @@ static tecoopsStatus_t flashAttentionCheckArgs(tecoopsHandle_t handle,
     if (bt->dimA[0] <= 0 || bt->dimA[1] <= 0 || q->dimA[1] <= 0 || k->dimA[1] <= 0 ||
         k->dimA[2] <= 0 || k->dimA[0] <= 0 || q->dimA[2] <= 0 || q->dimA[0] < 0)
         return TECOOPS_STATUS_BAD_PARAM;
-    if (q->dimA[1] % k->dimA[1] != 0) return TECOOPS_STATUS_BAD_PARAM;
+    const int hkv = layout == 1 ? k->dimA[2] : k->dimA[1];
+    if (q->dimA[1] % hkv != 0) return TECOOPS_STATUS_BAD_PARAM;
     if (q->dimA[2] > 256 || (q->dimA[2] & 1)) return TECOOPS_STATUS_NOT_SUPPORTED;
     if (!packed(q) || !packed(o) || !packed(k) || !packed(v) || !packed(bt))
         return TECOOPS_STATUS_NOT_SUPPORTED;
@@ -83,7 +93,7 @@ static void fillArgs(FlashAttentionArgs &a, tecoopsHandle_t handle, int max_seql
     a.batch_size = bt->dimA[0];
     a.size_per_head = q->dimA[2];
     a.local_head_num = q->dimA[1];
-    a.local_kv_head_num = k->dimA[1];
+    a.local_kv_head_num = k->dimA[1];   // reference layout; tecoopsFlashAttentionEx may swap
     a.block_size = k->dimA[2];
     a.block_table_dim = bt->dimA[1];
     a.max_q_seq_len = max_seqlen_q;
@@ -91,7 +101,7 @@ static void fillArgs(FlashAttentionArgs &a, tecoopsHandle_t handle, int max_seql
     a.max_block_num = k->dimA[0];
     a.total_q = q->dimA[0];
     a.softmax_scale = (float)(1.0 / std::sqrt((double)a.size_per_head));
-    a.dtype = k->dataType == TECOOPS_DATA_BFLOAT16 ? ElemType::BF16 : ElemType::F16;
+    a.dtype = q->dataType == TECOOPS_DATA_BFLOAT16 ? ElemType::BF16 : ElemType::F16;
     a.causal = 1;
     a.window_left = -1;
     a.window_right = -1;
@@ -99,6 +109,10 @@ static void fillArgs(FlashAttentionArgs &a, tecoopsHandle_t handle, int max_seql
     a.new_key = nullptr;
     a.new_value = nullptr;
     a.slot_mapping = nullptr;
+    a.kv_layout = 0;
+    a.cache_fp8 = 0;
+    a.k_scale = 1.f;
+    a.v_scale = 1.f;
 }
 
 extern "C" tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(
@@ -124,13 +138,19 @@ static tecoopsStatus_t flashAttentionImpl(
     const tecoopsTensorDescriptor_t vCacheDesc, const void *vCache,
     const tecoopsTensorDescriptor_t oDataDesc, void *oData, void *workspace,
     const tecoopsFlashAttentionOptions_t *options, float *softmax_lse) {
+    const int layout = options != nullptr ? options->kv_layout : 0;
+    if (layout != TECOOPS_KV_LAYOUT_HND && layout != TECOOPS_KV_LAYOUT_NHD)
+        return TECOOPS_STATUS_BAD_PARAM;
     tecoopsStatus_t st = flashAttentionCheckArgs(handle, blockTableDesc, qDataDesc, kCacheDesc,
-                                                 vCacheDesc, oDataDesc);
+                                                 vCacheDesc, oDataDesc, layout,
+                                                 options != nullptr);
     if (st != TECOOPS_STATUS_SUCCESS) return st;
     if (!q_seq_lens || !kv_seq_lens || !blockTable || !kCache || !vCache) return TECOOPS_STATUS_BAD_PARAM;
     if (qDataDesc->dimA[0] > 0 && (!qData || !oData)) return TECOOPS_STATUS_BAD_PARAM;
     if (max_seqlen_q < 0 || max_seqlen_k < 0) return TECOOPS_STATUS_BAD_PARAM;
-    if (options != nullptr && !(options->softmax_scale == options->softmax_scale))
+    if (options != nullptr &&
+        (!(options->softmax_scale == options->softmax_scale) ||
+         !(options->k_scale == options->k_scale) || !(options->v_scale == options->v_scale)))
         return TECOOPS_STATUS_BAD_PARAM;   // NaN scale
     if (qDataDesc->dimA[0] == 0 || max_seqlen_q == 0) return TECOOPS_STATUS_SUCCESS;
 
@@ -141,6 +161,14 @@ static tecoopsStatus_t flashAttentionImpl(
         args.causal = options->causal != 0 ? 1 : 0;
         args.window_left = options->window_left < 0 ? -1 : options->window_left;
         args.window_right = options->window_right < 0 ? -1 : options->window_right;
+        args.kv_layout = layout;
+        if (layout == TECOOPS_KV_LAYOUT_NHD) {
+            args.local_kv_head_num = kCacheDesc->dimA[2];
+            args.block_size = kCacheDesc->dimA[1];
+        }
+        args.cache_fp8 = kCacheDesc->dataType == TECOOPS_DATA_FLOAT8_E4M3 ? 1 : 0;
+        args.k_scale = options->k_scale > 0.f ? options->k_scale : 1.f;
+        args.v_scale = options->v_scale > 0.f ? options->v_scale : 1.f;
     }
     args.softmax_lse = softmax_lse;
     args.q_seq_lens = q_seq_lens;

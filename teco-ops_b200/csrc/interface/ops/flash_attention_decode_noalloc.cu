@@ -144,6 +144,9 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
     p.new_key = nullptr;
     p.new_value = nullptr;
     p.slot_mapping = nullptr;
+    p.kv_layout = 0;
+    p.cache_fp8 = 0;
+    p.v_scale = 1.f;
     const size_t need =
         tecoops::kern::decode_workspace_bytes(batch, heads, head_dim, p.max_splits);
     if (need > kNoAllocScratchBytes) {

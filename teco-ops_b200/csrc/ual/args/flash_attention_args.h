@@ -48,6 +48,12 @@ struct FlashAttentionArgs {
     const void *new_key;     // [total_q, Hkv, D] or null
     const void *new_value;
     const int64_t *slot_mapping;
+    // cache storage: 0 = [pages, Hkv, bs, D] (reference), 1 = [pages, bs, Hkv, D];
+    // cache_fp8: e4m3 elements dequantised as x * k_scale / x * v_scale
+    int kv_layout;
+    int cache_fp8;
+    float k_scale;
+    float v_scale;
 };
 
 // Branch selection input (reference FlashAttentionPatchArgs).

@@ -17,11 +17,15 @@ struct ReshapeAndCacheArgs {
     int size_per_head;   // head_size (elements)
     int num_blocks;
     int block_size;
-    int elem_bytes;      // 2 (fp16 / bf16)
-    // strides in elements
+    int elem_bytes;      // 2 (fp16 / bf16) for key/value and (unless cache_fp8) the caches
+    // cache_fp8: 0 = bit copy; 1 = e4m3(fp16 / scale); 2 = e4m3(bf16 / scale)
+    int cache_fp8;
+    float k_scale;
+    float v_scale;
+    // cache strides in cache elements (layout [NB, H, bs, D] or [NB, bs, H, D])
     int64_t block_stride;   // num_kv_heads * block_size * head_size
-    int64_t head_stride;    // block_size * head_size
-    int64_t entry_stride;   // head_size
+    int64_t head_stride;    // block_size * head_size   (D for [NB, bs, H, D])
+    int64_t entry_stride;   // head_size                (H * D for [NB, bs, H, D])
     int64_t key_stride;     // num_kv_heads * head_size (token stride of key)
     int64_t value_stride;   // token stride of value
     const void *key;

@@ -34,6 +34,13 @@
 //    overwrites that row of the staged K/V tiles from the new key/value, so the
 //    attention never depends on the ordering of the store and the TMA read of the
 //    same slot; one launch replaces the scatter kernel + decode.
+//  * cache layouts [pages, Hkv, bs, D] and [pages, bs, Hkv, D] differ only in the
+//    tensor maps' strides.  An e4m3 cache (FP8) is loaded raw (half the bytes) into
+//    the ring; each consumer warp converts its chunk to f16 (exact for e4m3) into a
+//    private 128B-swizzled staging tile, releases the ring stage at once and runs the
+//    same ldmatrix/MMA code in f16 (Q converted to f16 once).  k_scale is folded into
+//    the softmax scale and v_scale into the output.
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -55,16 +62,48 @@ constexpr int kStages = 8;        // multiple of the 4 consumer warps
 constexpr int kConsumers = 4;
 constexpr int kThreads = 32 * (kConsumers + 1);
 
-template <int D>
+template <int D, bool FP8>
 struct DecodeSmem {
     static constexpr int kHalves = D / 64;
     static constexpr int kHalfBytes = kChunk * 128;            // 16 rows x 64 columns
-    static constexpr int kTileBytes = kHalves * kHalfBytes;    // K or V of one chunk
-    static constexpr int kStageBytes = 2 * kTileBytes;
+    static constexpr int kTileBytes = kHalves * kHalfBytes;    // 16-bit K or V of one chunk
+    static constexpr int kRawTileBytes = FP8 ? kChunk * D : kTileBytes;   // as loaded
+    static constexpr int kStageBytes = 2 * kRawTileBytes;
     static constexpr int kRingBytes = kStages * kStageBytes;
+    // FP8: per consumer warp a 16-bit K and V staging tile after the ring
+    static constexpr int kStageTiles = FP8 ? kConsumers * 2 * kTileBytes : 0;
     static constexpr int kMergeBytes = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
-    static constexpr int kBytes = (kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes) + 1024;
+    static constexpr int kUsed = kRingBytes + kStageTiles;
+    static constexpr int kBytes = (kUsed > kMergeBytes ? kUsed : kMergeBytes) + 1024;
 };
+
+// 16 e4m3 bytes -> 16 f16 (two 16-byte chunks), exact
+__device__ __forceinline__ void e4m3x16_to_f16(const uint4 &in, uint4 &lo, uint4 &hi) {
+    const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2_raw a =
+            __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xffffu), __NV_E4M3);
+        const __half2_raw b =
+            __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
+        o[2 * i] = (uint32_t)a.x | ((uint32_t)a.y << 16);
+        o[2 * i + 1] = (uint32_t)b.x | ((uint32_t)b.y << 16);
+    }
+    lo = make_uint4(o[0], o[1], o[2], o[3]);
+    hi = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// bf16x2 / f16x2 word -> f16x2 word
+template <typename T>
+__device__ __forceinline__ uint32_t to_f16x2(uint32_t w) {
+    if constexpr (std::is_same<T, __half>::value) {
+        return w;
+    } else {
+        const float a = __uint_as_float(w << 16), b = __uint_as_float(w & 0xffff0000u);
+        return Elem<__half>::pack2(a, b);
+    }
+}
 
 // byte offset of 16-byte column chunk `ch` (0..D/8-1) of row `r` in a 128B-swizzled
 // [16][D] tile stored as D/64 halves of 16 rows x 128 bytes
@@ -74,15 +113,17 @@ __device__ __forceinline__ uint32_t swz128(int r, int ch) {
 
 }  // namespace
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 3)
+// FP8: 2 CTAs per SM (the conversion needs registers; a stage holds half the bytes)
+template <typename T, int D, bool FP8>
+__global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
     fa_decode_splitkv_kernel(const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, DecodeParams p) {
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[2 * kStages];
     __shared__ int abort_flag;
-    using Sm = DecodeSmem<D>;
+    using Sm = DecodeSmem<D, FP8>;
+    using MT = typename std::conditional<FP8, __half, T>::type;   // MMA operand type
 
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / p.num_slices;
@@ -104,14 +145,16 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int kv_end = min(kv_len, kv_begin + p.split_tokens);
     const int qrow = warp_seq_start(p.q_seq_lens, b);   // q_len == 1 on this path
     if (qrow >= p.total_q) return;                      // lengths beyond q's rows
-    const bool fused = p.new_key != nullptr;
+    const bool fused = !FP8 && p.new_key != nullptr;
     if (fused && slice == 0 && split == max(n_split_b, 1) - 1 && tid < D / 8) {
         // reshape_and_cache of the new token, this KV head: one 16-byte chunk per thread
         const int64_t slot = __ldg(p.slot_mapping + qrow);
         if (slot >= 0 && slot < (int64_t)p.num_pages * p.block_size) {
             const int64_t page = slot / p.block_size;
+            const int64_t row = slot - page * p.block_size;
             const int64_t dst =
-                ((page * p.num_kv_heads + kvh) * p.block_size + (slot - page * p.block_size)) * D;
+                (p.kv_layout == 0 ? (page * p.num_kv_heads + kvh) * p.block_size + row
+                                  : (page * p.block_size + row) * p.num_kv_heads + kvh) * D;
             const int64_t src = ((int64_t)qrow * p.num_kv_heads + kvh) * D;
             reinterpret_cast<uint4 *>(const_cast<void *>(p.key_cache))[(dst >> 3) + tid] =
                 __ldg(reinterpret_cast<const uint4 *>(p.new_key) + (src >> 3) + tid);
@@ -182,13 +225,18 @@ __global__ void __launch_bounds__(kThreads, 3)
                     if (ok) {
                         mbar_arrive_expect_tx(FULL(st), Sm::kStageBytes);
                         const uint32_t kd = sbase + st * Sm::kStageBytes;
-                        const uint32_t vd = kd + Sm::kTileBytes;
+                        const uint32_t vd = kd + Sm::kRawTileBytes;
+                        if (FP8) {   // one unswizzled box of 16 rows x D bytes
+                            tma_load_4d(kd, &kmap, FULL(st), 0, ri, kvh, bi);
+                            tma_load_4d(vd, &vmap, FULL(st), 0, ri, kvh, bi);
+                        } else {
 #pragma unroll
-                        for (int hh = 0; hh < Sm::kHalves; ++hh) {
-                            tma_load_4d(kd + hh * Sm::kHalfBytes, &kmap, FULL(st), hh * 64, ri,
-                                        kvh, bi);
-                            tma_load_4d(vd + hh * Sm::kHalfBytes, &vmap, FULL(st), hh * 64, ri,
-                                        kvh, bi);
+                            for (int hh = 0; hh < Sm::kHalves; ++hh) {
+                                tma_load_4d(kd + hh * Sm::kHalfBytes, &kmap, FULL(st), hh * 64,
+                                            ri, kvh, bi);
+                                tma_load_4d(vd + hh * Sm::kHalfBytes, &vmap, FULL(st), hh * 64,
+                                            ri, kvh, bi);
+                            }
                         }
                     }
                 }
@@ -219,6 +267,10 @@ __global__ void __launch_bounds__(kThreads, 3)
                 qa[kk][1] = g + 8 < rows ? __ldg(r1) : 0u;
                 qa[kk][2] = g < rows ? __ldg(r0 + 4) : 0u;
                 qa[kk][3] = g + 8 < rows ? __ldg(r1 + 4) : 0u;
+                if (FP8) {   // the MMAs run in f16 against the converted cache
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) qa[kk][i] = to_f16x2<T>(qa[kk][i]);
+                }
             }
         }
         const float sl2 = p.scale_log2;
@@ -229,12 +281,44 @@ __global__ void __launch_bounds__(kThreads, 3)
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(FULL(st), (ci / kStages) & 1, abortp,
                                                            p.dev_error, 0x1200 + (ci & 0xff))))
                 break;
-            const uint32_t ktile = sbase + st * Sm::kStageBytes;
-            const uint32_t vtile = ktile + Sm::kTileBytes;
             const int tok0 = kv_begin + ci * kChunk;
             const int nv = kv_end - tok0;   // tokens of this chunk before kv_end
             const int nlo = kv_lo - tok0;   // tokens of this chunk before the window
-            if (nv < kChunk) {
+            uint32_t ktile = sbase + st * Sm::kStageBytes;
+            uint32_t vtile = ktile + Sm::kRawTileBytes;
+            if (FP8) {
+                // convert the raw e4m3 chunk into this warp's 16-bit staging tiles (V rows
+                // past kv_len as zeros: their bytes may be NaN patterns), then free the stage
+                const uint32_t sk = sbase + Sm::kRingBytes + warp * 2 * Sm::kTileBytes;
+                const uint8_t *rk = sgen + (ktile - sbase);
+                const uint8_t *rv = rk + Sm::kRawTileBytes;
+                uint8_t *gk = sgen + (sk - sbase);
+                uint8_t *gv = gk + Sm::kTileBytes;
+                __syncwarp();   // the previous chunk's ldmatrix reads of the staging tiles
+#pragma unroll
+                for (int i = 0; i < (kChunk * D / 16) / 32; ++i) {
+                    const int idx = lane + 32 * i;
+                    const int r = idx / (D / 16);
+                    const int c16 = idx - r * (D / 16);
+                    uint4 lo, hi;
+                    e4m3x16_to_f16(*reinterpret_cast<const uint4 *>(rk + r * D + c16 * 16), lo, hi);
+                    *reinterpret_cast<uint4 *>(gk + swz128(r, 2 * c16)) = lo;
+                    *reinterpret_cast<uint4 *>(gk + swz128(r, 2 * c16 + 1)) = hi;
+                    if (r < nv) {
+                        e4m3x16_to_f16(*reinterpret_cast<const uint4 *>(rv + r * D + c16 * 16),
+                                       lo, hi);
+                    } else {
+                        lo = hi = make_uint4(0, 0, 0, 0);
+                    }
+                    *reinterpret_cast<uint4 *>(gv + swz128(r, 2 * c16)) = lo;
+                    *reinterpret_cast<uint4 *>(gv + swz128(r, 2 * c16 + 1)) = hi;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(EMPTY(st));
+                ktile = sk;
+                vtile = sk + Sm::kTileBytes;
+            }
+            if (!FP8 && nv < kChunk) {
                 // V rows past kv_len may hold arbitrary bits (unwritten slots): clear them
                 uint8_t *vt = sgen + (vtile - sbase);
                 for (int idx = lane; idx < (kChunk - nv) * (D / 8); idx += 32) {
@@ -267,8 +351,8 @@ __global__ void __launch_bounds__(kThreads, 3)
                 uint32_t kb[4];
                 const int r = (mi >> 1) * 8 + ri;
                 ldmatrix_x4(kb, ktile + swz128(r, 2 * kk + (mi & 1)));
-                mma16816<T>(s[0], qa[kk], kb[0], kb[1]);
-                mma16816<T>(s[1], qa[kk], kb[2], kb[3]);
+                mma16816<MT>(s[0], qa[kk], kb[0], kb[1]);
+                mma16816<MT>(s[1], qa[kk], kb[2], kb[3]);
             }
             float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
@@ -317,20 +401,22 @@ __global__ void __launch_bounds__(kThreads, 3)
                 }
             }
             uint32_t pa[4];
-            pa[0] = Elem<T>::pack2(s[0][0], s[0][1]);
-            pa[1] = Elem<T>::pack2(s[0][2], s[0][3]);
-            pa[2] = Elem<T>::pack2(s[1][0], s[1][1]);
-            pa[3] = Elem<T>::pack2(s[1][2], s[1][3]);
+            pa[0] = Elem<MT>::pack2(s[0][0], s[0][1]);
+            pa[1] = Elem<MT>::pack2(s[0][2], s[0][3]);
+            pa[2] = Elem<MT>::pack2(s[1][0], s[1][1]);
+            pa[3] = Elem<MT>::pack2(s[1][2], s[1][3]);
 #pragma unroll
             for (int nn = 0; nn < D / 16; ++nn) {
                 uint32_t vb[4];
                 const int r = (mi & 1) * 8 + ri;
                 ldmatrix_x4_trans(vb, vtile + swz128(r, 2 * nn + (mi >> 1)));
-                mma16816<T>(o[2 * nn], pa, vb[0], vb[1]);
-                mma16816<T>(o[2 * nn + 1], pa, vb[2], vb[3]);
+                mma16816<MT>(o[2 * nn], pa, vb[0], vb[1]);
+                mma16816<MT>(o[2 * nn + 1], pa, vb[2], vb[3]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(EMPTY(st));
+            if (!FP8) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(EMPTY(st));
+            }
         }
         l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
         l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
@@ -375,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 3)
             L += sml[(w * 16 + r) * 2 + 1] * f;
             O += so[(w * 16 + r) * D + d] * f;
         }
-        const float val = L > 0.f ? O / L : 0.f;
+        const float val = (L > 0.f ? O / L : 0.f) * (FP8 ? p.v_scale : 1.f);
         const int h = head0 + r;
         if (direct) {
             T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * D + d;
@@ -416,7 +502,7 @@ __global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
             O += w * p.part_o[(rec0 + s) * p.head_dim + d];
         }
         T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * p.head_dim + d;
-        *out = Elem<T>::from_float(W > 0.f ? O / W : 0.f);
+        *out = Elem<T>::from_float(W > 0.f ? O / W : 0.f);   // partials carry v_scale
         if (p.lse != nullptr && d == 0)
             p.lse[(int64_t)h * p.total_q + qrow] =
                 W > 0.f ? (Mu + log2f(W)) * 0.6931471805599453f : -INFINITY;
@@ -450,17 +536,18 @@ size_t decode_workspace_bytes(int batch, int num_heads, int head_dim, int max_sp
     return recs * head_dim * sizeof(float) + recs * sizeof(float) + 256;
 }
 
-template <typename T, int D>
+template <typename T, int D, bool FP8>
 static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
-    const bool bf16 = !std::is_same<T, __half>::value;
+    const CacheElem ce = FP8 ? CacheElem::E4M3
+                             : std::is_same<T, __half>::value ? CacheElem::F16 : CacheElem::BF16;
     CUtensorMap kmap, vmap;
-    if (!encode_cache_map(&kmap, p.key_cache, bf16, D, p.block_size, p.num_kv_heads,
-                          p.num_pages, kChunk) ||
-        !encode_cache_map(&vmap, p.value_cache, bf16, D, p.block_size, p.num_kv_heads,
-                          p.num_pages, kChunk))
+    if (!encode_cache_map(&kmap, p.key_cache, ce, D, p.block_size, p.num_kv_heads, p.num_pages,
+                          kChunk, p.kv_layout) ||
+        !encode_cache_map(&vmap, p.value_cache, ce, D, p.block_size, p.num_kv_heads,
+                          p.num_pages, kChunk, p.kv_layout))
         return cudaErrorInvalidValue;
-    const int smem = DecodeSmem<D>::kBytes;
-    auto kfn = fa_decode_splitkv_kernel<T, D>;
+    const int smem = DecodeSmem<D, FP8>::kBytes;
+    auto kfn = fa_decode_splitkv_kernel<T, D, FP8>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p.max_splits, p.num_kv_heads * p.num_slices, p.batch);
@@ -474,16 +561,23 @@ static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
     return e;
 }
 
-cudaError_t launch_decode(const DecodeParams &p, bool bf16, cudaStream_t stream) {
+template <bool FP8>
+static cudaError_t launch_decode_f(const DecodeParams &p, bool bf16, cudaStream_t stream) {
     if (p.head_dim == 128) {
-        return bf16 ? launch_decode_t<__nv_bfloat16, 128>(p, stream)
-                    : launch_decode_t<__half, 128>(p, stream);
+        return bf16 ? launch_decode_t<__nv_bfloat16, 128, FP8>(p, stream)
+                    : launch_decode_t<__half, 128, FP8>(p, stream);
     }
     if (p.head_dim == 64) {
-        return bf16 ? launch_decode_t<__nv_bfloat16, 64>(p, stream)
-                    : launch_decode_t<__half, 64>(p, stream);
+        return bf16 ? launch_decode_t<__nv_bfloat16, 64, FP8>(p, stream)
+                    : launch_decode_t<__half, 64, FP8>(p, stream);
     }
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_decode(const DecodeParams &p, bool bf16, cudaStream_t stream) {
+    if (p.cache_fp8 && p.new_key != nullptr) return cudaErrorInvalidValue;
+    return p.cache_fp8 ? launch_decode_f<true>(p, bf16, stream)
+                       : launch_decode_f<false>(p, bf16, stream);
 }
 
 }  // namespace kern

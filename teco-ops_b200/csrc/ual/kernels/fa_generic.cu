@@ -11,10 +11,14 @@
 // lane for the dot product, then the lanes switch to owning head dimensions for
 // the P.V accumulation; online softmax in the exp2 domain.  The options of
 // tecoopsFlashAttentionEx (scale, causal, window, log-sum-exp output) bound the
-// key range [lo, end) of each row.
+// key range [lo, end) of each row.  Caches in either page layout, 16-bit or e4m3
+// (dequantised with k_scale / v_scale).
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdint>
+#include <type_traits>
 
 #include "ual/kernels/common.cuh"
 #include "ual/kernels/launchers.h"
@@ -22,7 +26,19 @@
 namespace tecoops {
 namespace kern {
 
-template <typename T>
+// cache element -> float (e4m3: exact via f16, times the scale)
+template <typename T, typename C>
+__device__ __forceinline__ float cache_to_float(C x, float scale) {
+    if constexpr (std::is_same<C, uint8_t>::value) {
+        const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)x, __NV_E4M3);
+        return __half2float(__half(h)) * scale;
+    } else {
+        (void)scale;
+        return Elem<T>::to_float(x);
+    }
+}
+
+template <typename T, typename C>
 __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
     constexpr int kMaxD = 256;
     __shared__ float qs[4][kMaxD];
@@ -61,11 +77,14 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
     for (int d = lane; d < D; d += 32) qs[warp][d] = Elem<T>::to_float(q[d]);
     __syncwarp();
 
-    const T *kc = static_cast<const T *>(s.key_cache);
-    const T *vc = static_cast<const T *>(s.value_cache);
+    const C *kc = static_cast<const C *>(s.key_cache);
+    const C *vc = static_cast<const C *>(s.value_cache);
     const int *bt = s.block_table + (int64_t)b * s.block_table_dim;
     const int64_t page_stride = (int64_t)s.num_kv_heads * s.block_size * D;
-    const int64_t head_off = (int64_t)kvh * s.block_size * D;
+    // [pages, Hkv, bs, D] or [pages, bs, Hkv, D]
+    const int64_t head_off = s.kv_layout == 0 ? (int64_t)kvh * s.block_size * D : (int64_t)kvh * D;
+    const int64_t row_stride = s.kv_layout == 0 ? D : (int64_t)s.num_kv_heads * D;
+    const float ks = s.cache_fp8 ? s.k_scale : 1.f, vs = s.cache_fp8 ? s.v_scale : 1.f;
 
     float m = -INFINITY, l = 0.f;
     float acc[kMaxD / 32];
@@ -79,9 +98,9 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
         if (j < end) {
             int blk = __ldg(bt + j / s.block_size);
             if (blk < 0 || blk >= s.num_pages) blk = 0;   // bad page id: stay in bounds
-            my_off = (int64_t)blk * page_stride + head_off + (int64_t)(j % s.block_size) * D;
+            my_off = (int64_t)blk * page_stride + head_off + (int64_t)(j % s.block_size) * row_stride;
             float dot = 0.f;
-            for (int d = 0; d < D; ++d) dot += qs[warp][d] * Elem<T>::to_float(kc[my_off + d]);
+            for (int d = 0; d < D; ++d) dot += qs[warp][d] * cache_to_float<T>(kc[my_off + d], ks);
             x = dot * s.scale_log2;
         }
         float cm = x;
@@ -104,7 +123,7 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(AttnShape s) {
 #pragma unroll
             for (int k = 0; k < kMaxD / 32; ++k) {
                 const int d = lane + 32 * k;
-                if (d < D) acc[k] += pt * Elem<T>::to_float(vc[off + d]);
+                if (d < D) acc[k] += pt * cache_to_float<T>(vc[off + d], vs);
             }
         }
     }
@@ -124,10 +143,16 @@ cudaError_t launch_generic_attention(const AttnShape &s, bool bf16, cudaStream_t
     const int64_t pairs = (int64_t)s.total_q * s.num_heads;
     if (pairs == 0) return cudaSuccess;
     const unsigned grid = (unsigned)((pairs + 3) / 4);
-    if (bf16)
-        fa_generic_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(s);
-    else
-        fa_generic_kernel<__half><<<grid, 128, 0, stream>>>(s);
+    if (s.cache_fp8) {
+        if (bf16)
+            fa_generic_kernel<__nv_bfloat16, uint8_t><<<grid, 128, 0, stream>>>(s);
+        else
+            fa_generic_kernel<__half, uint8_t><<<grid, 128, 0, stream>>>(s);
+    } else if (bf16) {
+        fa_generic_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 128, 0, stream>>>(s);
+    } else {
+        fa_generic_kernel<__half, __half><<<grid, 128, 0, stream>>>(s);
+    }
     return cudaGetLastError();
 }
 

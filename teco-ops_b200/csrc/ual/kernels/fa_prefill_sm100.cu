@@ -52,6 +52,7 @@
 #include "ual/kernels/common.cuh"
 #include "ual/kernels/launchers.h"
 #include "ual/kernels/sm100_primitives.cuh"
+#include "ual/kernels/tensor_map.h"
 
 namespace tecoops {
 namespace kern {
@@ -797,27 +798,6 @@ extern "C" int tecoops_prefill_trace_read(long long *host, size_t n) {
 
 // ---- host side ------------------------------------------------------------------------
 
-typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                    const cuuint32_t *, CUtensorMapInterleave,
-                                    CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                    CUtensorMapFloatOOBfill);
-
-static PFN_encodeTiled get_encode_fn() {
-    static PFN_encodeTiled fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void *ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_encodeTiled>(ptr);
-    }
-    return fn;
-}
-
 bool prefill_supported(int head_dim, int block_size, int group) {
     (void)group;
     if (head_dim != 64 && head_dim != 128) return false;
@@ -851,21 +831,11 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, int num_
     }
     const int rpb = s.block_size < 128 ? s.block_size : 128;
     {
-        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)s.block_size,
-                              (cuuint64_t)s.num_kv_heads, (cuuint64_t)s.num_pages};
-        cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)s.block_size * D * 2,
-                                 (cuuint64_t)s.num_kv_heads * s.block_size * D * 2};
-        cuuint32_t box[4] = {64, (cuuint32_t)rpb, 1, 1};
-        cuuint32_t es[4] = {1, 1, 1, 1};
-        if (enc(&kmap, dt, 4, const_cast<void *>(s.key_cache), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-        if (enc(&vmap, dt, 4, const_cast<void *>(s.value_cache), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        const CacheElem ce = std::is_same<T, __half>::value ? CacheElem::F16 : CacheElem::BF16;
+        if (!encode_cache_map(&kmap, s.key_cache, ce, D, s.block_size, s.num_kv_heads,
+                              s.num_pages, rpb, s.kv_layout) ||
+            !encode_cache_map(&vmap, s.value_cache, ce, D, s.block_size, s.num_kv_heads,
+                              s.num_pages, rpb, s.kv_layout))
             return cudaErrorInvalidValue;
     }
     PrefillParams p;

@@ -45,6 +45,10 @@ struct AttnShape {
     int window_left;
     int window_right;
     float *lse;               // optional [Hq, total_q] natural-log log-sum-exp
+    int kv_layout;            // 0: [pages, Hkv, bs, D]; 1: [pages, bs, Hkv, D]
+    int cache_fp8;            // e4m3 cache elements, dequantised with k_scale / v_scale
+    float k_scale;
+    float v_scale;
 };
 
 // ---- split-KV decode -------------------------------------------------------------
@@ -80,6 +84,9 @@ struct DecodeParams {
     const void *new_key;
     const void *new_value;
     const int64_t *slot_mapping;
+    int kv_layout;      // 0: [pages, Hkv, bs, D]; 1: [pages, bs, Hkv, D]
+    int cache_fp8;      // e4m3 cache: K*k_scale folded into scale_log2, O *= v_scale
+    float v_scale;
 };
 
 bool decode_supported(int head_dim, int block_size, int group);

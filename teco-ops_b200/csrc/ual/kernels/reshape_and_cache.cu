@@ -16,9 +16,18 @@
 // same 256-byte head row, so both the reads and the scattered writes are whole
 // 32-byte sectors.  The grid is a multiple of the SM count.  64-bit offsets
 // throughout (caches beyond 2^31 elements).
+//
+// Extensions: the cache strides cover both page layouts ([NB, H, bs, D] and
+// vLLM's [NB, bs, H, D]); an e4m3 cache stores e4m3(x / scale) with IEEE division
+// and round-to-nearest-even, saturated to the finite range (+-448), 16 elements
+// per thread (32 bytes read, 16 written).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "ual/args/reshape_and_cache_args.h"
 
@@ -113,13 +122,147 @@ __global__ void __launch_bounds__(256) reshape_and_cache_u16_kernel(
     }
 }
 
+template <typename Tin>
+__device__ __forceinline__ float in_to_float(Tin x) {
+    if constexpr (std::is_same<Tin, __half>::value)
+        return __half2float(x);
+    else
+        return __bfloat162float(x);
+}
+
+// two floats -> e4m3x2 (first value in the low byte), saturating
+__device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
+    return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+}
+
+// 8 consecutive 16-bit inputs (one 16-byte vector) / scale -> 8 e4m3 bytes
+template <typename Tin>
+__device__ __forceinline__ uint2 quant8(const uint4 &v, float scale) {
+    const Tin *e = reinterpret_cast<const Tin *>(&v);
+    uint32_t w[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t p0 = e4m3x2(__fdiv_rn(in_to_float(e[4 * i]), scale),
+                                   __fdiv_rn(in_to_float(e[4 * i + 1]), scale));
+        const uint32_t p1 = e4m3x2(__fdiv_rn(in_to_float(e[4 * i + 2]), scale),
+                                   __fdiv_rn(in_to_float(e[4 * i + 3]), scale));
+        w[i] = p0 | (p1 << 16);
+    }
+    return make_uint2(w[0], w[1]);
+}
+
+// e4m3 cache, vectorised: one unit = 16 elements of one (token, head) row.
+// Strides: key/value in elements (16-bit), cache in bytes.
+template <typename Tin>
+__global__ void __launch_bounds__(256) reshape_and_cache_fp8_kernel(
+    const uint8_t *__restrict__ key, const uint8_t *__restrict__ value,
+    const int64_t *__restrict__ slot_mapping, uint8_t *__restrict__ key_cache,
+    uint8_t *__restrict__ value_cache, int64_t total_units, int units_per_head, int heads,
+    int block_size, int64_t num_slots, int64_t key_stride, int64_t value_stride,
+    int64_t block_stride, int64_t head_stride, int64_t entry_stride, float k_scale,
+    float v_scale) {
+    const int64_t units_per_token = (int64_t)units_per_head * heads;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total_units;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / units_per_token;
+        const int r = (int)(i - t * units_per_token);
+        const int h = r / units_per_head;
+        const int c = r - h * units_per_head;
+        const int64_t slot = __ldg(slot_mapping + t);
+        if (slot < 0 || slot >= num_slots) continue;
+        const int64_t blk = slot / block_size;
+        const int64_t off = slot - blk * block_size;
+        const int64_t dst = blk * block_stride + h * head_stride + off * entry_stride + c * 16;
+        const uint8_t *kp = key + (t * key_stride + (int64_t)r * 16) * 2;
+        const uint8_t *vp = value + (t * value_stride + (int64_t)r * 16) * 2;
+        const uint2 k0 = quant8<Tin>(ld_stream16(kp), k_scale);
+        const uint2 k1 = quant8<Tin>(ld_stream16(kp + 16), k_scale);
+        const uint2 v0 = quant8<Tin>(ld_stream16(vp), v_scale);
+        const uint2 v1 = quant8<Tin>(ld_stream16(vp + 16), v_scale);
+        st16(key_cache + dst, make_uint4(k0.x, k0.y, k1.x, k1.y));
+        st16(value_cache + dst, make_uint4(v0.x, v0.y, v1.x, v1.y));
+    }
+}
+
+// e4m3 cache, any head_size / alignment: one element per thread
+template <typename Tin>
+__global__ void __launch_bounds__(256) reshape_and_cache_fp8_scalar_kernel(
+    const Tin *__restrict__ key, const Tin *__restrict__ value,
+    const int64_t *__restrict__ slot_mapping, uint8_t *__restrict__ key_cache,
+    uint8_t *__restrict__ value_cache, int64_t total, int head_size, int heads, int block_size,
+    int64_t num_slots, int64_t key_stride, int64_t value_stride, int64_t block_stride,
+    int64_t head_stride, int64_t entry_stride, float k_scale, float v_scale) {
+    const int64_t per_token = (int64_t)head_size * heads;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / per_token;
+        const int r = (int)(i - t * per_token);
+        const int h = r / head_size;
+        const int d = r - h * head_size;
+        const int64_t slot = __ldg(slot_mapping + t);
+        if (slot < 0 || slot >= num_slots) continue;
+        const int64_t blk = slot / block_size;
+        const int64_t off = slot - blk * block_size;
+        const int64_t o = blk * block_stride + h * head_stride + off * entry_stride + d;
+        key_cache[o] = (uint8_t)(e4m3x2(__fdiv_rn(in_to_float(key[t * key_stride + r]), k_scale),
+                                        0.f) & 0xffu);
+        value_cache[o] = (uint8_t)(
+            e4m3x2(__fdiv_rn(in_to_float(value[t * value_stride + r]), v_scale), 0.f) & 0xffu);
+    }
+}
+
 static inline bool aligned16(const void *p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+static cudaError_t launch_fp8(const ReshapeAndCacheArgs &a, int num_sms, cudaStream_t stream) {
+    const int64_t num_slots = (int64_t)a.num_blocks * a.block_size;
+    const float ks = a.k_scale > 0.f ? a.k_scale : 1.f, vs = a.v_scale > 0.f ? a.v_scale : 1.f;
+    const bool vec = (a.size_per_head % 16 == 0) && aligned16(a.key) && aligned16(a.value) &&
+                     aligned16(a.key_cache) && aligned16(a.value_cache) &&
+                     ((a.key_stride * 2) % 16 == 0) && ((a.value_stride * 2) % 16 == 0) &&
+                     (a.block_stride % 16 == 0) && (a.head_stride % 16 == 0) &&
+                     (a.entry_stride % 16 == 0);
+    const int64_t cap = (int64_t)num_sms * 8;
+    if (vec) {
+        const int uph = a.size_per_head / 16;
+        const int64_t total = (int64_t)a.num_tokens * a.num_kv_heads * uph;
+        int64_t grid = (total + 255) / 256;
+        if (grid > cap) grid = cap;
+        auto kfn = a.cache_fp8 == 2 ? reshape_and_cache_fp8_kernel<__nv_bfloat16>
+                                    : reshape_and_cache_fp8_kernel<__half>;
+        kfn<<<(unsigned)grid, 256, 0, stream>>>(
+            static_cast<const uint8_t *>(a.key), static_cast<const uint8_t *>(a.value),
+            a.slot_mapping, static_cast<uint8_t *>(a.key_cache),
+            static_cast<uint8_t *>(a.value_cache), total, uph, a.num_kv_heads, a.block_size,
+            num_slots, a.key_stride, a.value_stride, a.block_stride, a.head_stride,
+            a.entry_stride, ks, vs);
+    } else {
+        const int64_t total = (int64_t)a.num_tokens * a.num_kv_heads * a.size_per_head;
+        int64_t grid = (total + 255) / 256;
+        if (grid > cap) grid = cap;
+        if (a.cache_fp8 == 2)
+            reshape_and_cache_fp8_scalar_kernel<__nv_bfloat16><<<(unsigned)grid, 256, 0, stream>>>(
+                static_cast<const __nv_bfloat16 *>(a.key),
+                static_cast<const __nv_bfloat16 *>(a.value), a.slot_mapping,
+                static_cast<uint8_t *>(a.key_cache), static_cast<uint8_t *>(a.value_cache), total,
+                a.size_per_head, a.num_kv_heads, a.block_size, num_slots, a.key_stride,
+                a.value_stride, a.block_stride, a.head_stride, a.entry_stride, ks, vs);
+        else
+            reshape_and_cache_fp8_scalar_kernel<__half><<<(unsigned)grid, 256, 0, stream>>>(
+                static_cast<const __half *>(a.key), static_cast<const __half *>(a.value),
+                a.slot_mapping, static_cast<uint8_t *>(a.key_cache),
+                static_cast<uint8_t *>(a.value_cache), total, a.size_per_head, a.num_kv_heads,
+                a.block_size, num_slots, a.key_stride, a.value_stride, a.block_stride,
+                a.head_stride, a.entry_stride, ks, vs);
+    }
+    return cudaGetLastError();
 }
 
 cudaError_t launch_reshape_and_cache(const ReshapeAndCacheArgs &a, int num_sms,
                                      cudaStream_t stream) {
     if (a.num_tokens <= 0) return cudaSuccess;
+    if (a.cache_fp8) return launch_fp8(a, num_sms, stream);
     const int eb = a.elem_bytes;
     const int64_t num_slots = (int64_t)a.num_blocks * a.block_size;
     const int row_bytes = a.size_per_head * eb;

@@ -29,22 +29,43 @@ inline PFN_encodeTiled get_encode_fn() {
     return fn;
 }
 
-// 4-D map over a cache [pages, Hkv, block_size, D] of 2-byte elements with a box
-// of {64 columns, box_rows rows, 1 head, 1 page} and 128-byte swizzle.  Page ids are
-// TMA coordinates, so an out-of-range page reads as zeros.
-inline bool encode_cache_map(CUtensorMap *map, const void *base, bool bf16, int head_dim,
-                             int block_size, int kv_heads, int pages, int box_rows) {
+// Cache element types of a tensor map.
+enum class CacheElem { F16, BF16, E4M3 };
+
+// 4-D map over a paged cache with coordinates (column, row in page, kv head, page):
+//   layout 0: [pages, Hkv, block_size, D]   layout 1: [pages, block_size, Hkv, D]
+// (the strides differ, the coordinate order does not, so kernels are layout-blind).
+// Box {box_cols, box_rows, 1, 1}; 16-bit caches use 64-column boxes with 128-byte
+// swizzle, e4m3 caches one unswizzled box of D bytes per row.  Page ids are TMA
+// coordinates, so an out-of-range page reads as zeros.
+inline bool encode_cache_map(CUtensorMap *map, const void *base, CacheElem elem, int head_dim,
+                             int block_size, int kv_heads, int pages, int box_rows,
+                             int layout) {
     PFN_encodeTiled enc = get_encode_fn();
     if (!enc) return false;
+    const cuuint64_t eb = elem == CacheElem::E4M3 ? 1 : 2;
+    const cuuint64_t row_b = (cuuint64_t)head_dim * eb;
     cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)block_size, (cuuint64_t)kv_heads,
                           (cuuint64_t)pages};
-    cuuint64_t strides[3] = {(cuuint64_t)head_dim * 2, (cuuint64_t)block_size * head_dim * 2,
-                             (cuuint64_t)kv_heads * block_size * head_dim * 2};
-    cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+    cuuint64_t strides[3];
+    if (layout == 0) {
+        strides[0] = row_b;                                  // row in page
+        strides[1] = (cuuint64_t)block_size * row_b;         // kv head
+    } else {
+        strides[0] = (cuuint64_t)kv_heads * row_b;           // row in page
+        strides[1] = row_b;                                  // kv head
+    }
+    strides[2] = (cuuint64_t)kv_heads * block_size * row_b;  // page
+    const bool fp8 = elem == CacheElem::E4M3;
+    cuuint32_t box[4] = {fp8 ? (cuuint32_t)head_dim : 64u, (cuuint32_t)box_rows, 1, 1};
     cuuint32_t es[4] = {1, 1, 1, 1};
-    return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-               const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : elem == CacheElem::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return enc(map, dt, 4, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE,
+               fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

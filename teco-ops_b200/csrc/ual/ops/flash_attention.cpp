@@ -37,6 +37,10 @@ static kern::AttnShape toShape(const FlashAttentionArgs &a) {
     s.window_left = a.window_left;
     s.window_right = a.window_right;
     s.lse = a.softmax_lse;
+    s.kv_layout = a.kv_layout;
+    s.cache_fp8 = a.cache_fp8;
+    s.k_scale = a.k_scale;
+    s.v_scale = a.v_scale;
     return s;
 }
 
@@ -65,7 +69,11 @@ static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
     p.num_pages = a.max_block_num;
     p.total_q = a.total_q;
     decodePlan(a, &p.split_tokens, &p.max_splits);
-    p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    // an e4m3 cache's k_scale multiplies every score: folded into the softmax scale
+    p.scale_log2 = a.softmax_scale * (a.cache_fp8 ? a.k_scale : 1.f) * 1.4426950408889634f;
+    p.kv_layout = a.kv_layout;
+    p.cache_fp8 = a.cache_fp8;
+    p.v_scale = a.cache_fp8 ? a.v_scale : 1.f;
     p.part_o = nullptr;
     p.part_lse = nullptr;
     p.dev_error = a.dev_error;
@@ -98,7 +106,8 @@ FlashAttentionAlgos FlashAttentionOp::selectAlgo(const FlashAttentionArgs &a) {
     const int group = a.local_head_num / a.local_kv_head_num;
     if (a.max_q_seq_len == 1 && kern::decode_supported(a.size_per_head, a.block_size, group))
         return FlashAttentionAlgos::DECODE_SPLITKV;
-    if (kern::prefill_supported(a.size_per_head, a.block_size, group))
+    // the tcgen05 prefill reads 16-bit caches only; e4m3 caches prefill generically
+    if (!a.cache_fp8 && kern::prefill_supported(a.size_per_head, a.block_size, group))
         return FlashAttentionAlgos::PREFILL_TCGEN05;
     return FlashAttentionAlgos::GENERIC;
 }

@@ -18,6 +18,9 @@ SUCCESS, NOT_INITIALIZED, ALLOC_FAILED, BAD_PARAM, INTERNAL_ERROR, INVALID_VALUE
 # tecoopsDataType_t
 DATA_FLOAT, DATA_HALF, DATA_INT8, DATA_INT16, DATA_INT32, DATA_INT64, DATA_UINT8, DATA_BOOL, \
     DATA_DOUBLE, DATA_BFLOAT16, DATA_COMPLEX_FLOAT = range(11)
+DATA_FLOAT8_E4M3 = 32   # extension: e4m3 KV cache
+# tecoopsKvLayout_t
+KV_LAYOUT_HND, KV_LAYOUT_NHD = 0, 1
 # tecoopsTensorFormat_t
 TENSOR_NCHW, TENSOR_NHWC, TENSOR_CHWN, TENSOR_NWHC = range(4)
 
@@ -27,7 +30,7 @@ EXPORTED = [
     "tecoopsGetErrorString", "tecoopsCreateTensorDescriptor", "tecoopsSetTensor4dDescriptor",
     "tecoopsGetTensor4dDescriptor", "tecoopsSetTensorNdDescriptor",
     "tecoopsGetTensorNdDescriptor", "tecoopsDestroyTensorDescriptor", "tecoopsMemset",
-    "tecoopsReshapeAndCache", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
+    "tecoopsReshapeAndCache", "tecoopsReshapeAndCacheEx", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
     "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlashAttentionEx",
     "tecoopsReshapeAndCacheFlashAttentionDecode", "tecoopsFlattenRays", "tecoopsReduceVariance",
     "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsCausalConv1d",
@@ -41,7 +44,14 @@ _lib = None
 class FlashAttentionOptions(ctypes.Structure):
     """tecoopsFlashAttentionOptions_t."""
     _fields_ = [("softmax_scale", ctypes.c_float), ("causal", _i), ("window_left", _i),
-                ("window_right", _i)]
+                ("window_right", _i), ("kv_layout", _i), ("k_scale", ctypes.c_float),
+                ("v_scale", ctypes.c_float)]
+
+
+class KvCacheConfig(ctypes.Structure):
+    """tecoopsKvCacheConfig_t."""
+    _fields_ = [("kv_layout", _i), ("cache_dtype", _i), ("k_scale", ctypes.c_float),
+                ("v_scale", ctypes.c_float)]
 
 
 class TecoopsError(RuntimeError):
@@ -72,6 +82,8 @@ def lib():
         "tecoopsDestroyTensorDescriptor": [_vp],
         "tecoopsMemset": [_vp, _vp, _i, ctypes.c_size_t],
         "tecoopsReshapeAndCache": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i],
+        "tecoopsReshapeAndCacheEx": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                                     ctypes.POINTER(KvCacheConfig)],
         "tecoopsFlashAttention": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                   _vp, _vp, _vp, _vp],
         "tecoopsGetFlashAttentionWorkspaceSize": [_vp, _i, _i, _vp, _vp, _vp,
@@ -155,6 +167,20 @@ def reshape_and_cache(handle: Handle, key, value, slot_mapping, key_cache, value
                                         num_kv_heads, head_size, num_blocks, block_size)
 
 
+def reshape_and_cache_ex(handle: Handle, key, value, slot_mapping, key_cache, value_cache,
+                         num_tokens, num_kv_heads, head_size, num_blocks, block_size, key_dtype,
+                         kv_layout=KV_LAYOUT_HND, cache_dtype=None, k_scale=1.0,
+                         v_scale=1.0) -> int:
+    """tecoopsReshapeAndCacheEx: page layout and e4m3 caches (cache_dtype
+    DATA_FLOAT8_E4M3 stores e4m3(x / scale))."""
+    cfg = KvCacheConfig(int(kv_layout), int(key_dtype if cache_dtype is None else cache_dtype),
+                        float(k_scale), float(v_scale))
+    return lib().tecoopsReshapeAndCacheEx(handle.h, _vp(key), _vp(value), _vp(slot_mapping),
+                                          _vp(key_cache), _vp(value_cache), num_tokens,
+                                          num_kv_heads, head_size, num_blocks, block_size,
+                                          int(key_dtype), ctypes.byref(cfg))
+
+
 def flash_attention(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num, q_seq_lens,
                     kv_seq_lens, bt_desc: Desc, block_table, q_desc: Desc, q, k_desc: Desc,
                     k_cache, v_desc: Desc, v_cache, o_desc: Desc, out, workspace=0) -> int:
@@ -168,11 +194,13 @@ def flash_attention(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num, q
 def flash_attention_ex(handle: Handle, max_seqlen_q, max_seqlen_k, max_block_num, q_seq_lens,
                        kv_seq_lens, bt_desc: Desc, block_table, q_desc: Desc, q, k_desc: Desc,
                        k_cache, v_desc: Desc, v_cache, o_desc: Desc, out, workspace=0,
-                       softmax_scale=0.0, causal=True, window=(-1, -1), softmax_lse=0) -> int:
+                       softmax_scale=0.0, causal=True, window=(-1, -1), softmax_lse=0,
+                       kv_layout=KV_LAYOUT_HND, k_scale=1.0, v_scale=1.0) -> int:
     """tecoopsFlashAttentionEx: scale (<= 0: 1/sqrt(D)), causal, window (left, right;
-    negative = unbounded) and an optional fp32 [Hq, total_q] log-sum-exp output."""
+    negative = unbounded), an optional fp32 [Hq, total_q] log-sum-exp output, the cache
+    page layout and (e4m3 cache descriptors) the dequantisation scales."""
     opts = FlashAttentionOptions(float(softmax_scale), 1 if causal else 0, int(window[0]),
-                                 int(window[1]))
+                                 int(window[1]), int(kv_layout), float(k_scale), float(v_scale))
     return lib().tecoopsFlashAttentionEx(handle.h, max_seqlen_q, max_seqlen_k, max_block_num,
                                          _vp(q_seq_lens), _vp(kv_seq_lens), bt_desc.d,
                                          _vp(block_table), q_desc.d, _vp(q), k_desc.d,

@@ -137,3 +137,25 @@ def test_oracle_window_properties():
         oracle.flash_attn_varlen(q, kc, vc, L, S, bt, window=(10_000, -1)), base)
     np.testing.assert_array_equal(
         oracle.flash_attn_varlen(q, kc, vc, L, S, bt, causal=False, window=(-1, 0)), base)
+
+
+def test_fp8_oracle_matches_torch_e4m3():
+    """oracle.fp8 (restated OCP E4M3, round-to-nearest-even) against torch's
+    float8_e4m3fn conversion on random values, every code point and every tie."""
+    import torch
+    from oracle import fp8
+    rng = np.random.default_rng(0)
+    vals = fp8.E4M3_VALUES[:127].astype(np.float32)
+    ties = ((fp8.E4M3_VALUES[:126] + fp8.E4M3_VALUES[1:127]) / 2).astype(np.float32)
+    x = np.concatenate([rng.standard_normal(100_000).astype(np.float32) * 60, vals, -vals, ties,
+                        -ties])
+    x = x[np.abs(x) <= 448]
+    t = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(fp8.encode(x), t)
+    # finite saturation and NaN
+    assert fp8.encode(np.array([1e6, -1e6, 449.0], np.float32)).tolist() == [0x7E, 0xFE, 0x7E]
+    assert fp8.encode(np.array([np.nan], np.float32))[0] == 0x7F
+    codes = np.arange(256, dtype=np.uint8)
+    ok = ~np.isnan(fp8.decode(codes))
+    assert np.array_equal(fp8.encode(fp8.decode(codes))[ok], codes[ok] & np.where(
+        codes[ok] == 0x80, 0xFF, 0xFF).astype(np.uint8))

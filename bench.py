@@ -273,6 +273,39 @@ class Workloads:
             self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr())
         self.capi.check(st, "reshape_and_cache_flash_attention_decode")
 
+    # ---- config 3 on an e4m3 cache (extension): same shapes, half the cache bytes
+    def setup_decode_fp8(self):
+        torch, capi = self.torch, self.capi
+        self.f_ks, self.f_vs = 1.0 / 64, 1.0 / 64
+        self.f_kc = (self.d_kc.float() / self.f_ks).to(torch.float8_e4m3fn).view(torch.uint8)
+        self.f_vc = (self.d_vc.float() / self.f_vs).to(torch.float8_e4m3fn).view(torch.uint8)
+        self.f_desc = capi.Desc(capi.DATA_FLOAT8_E4M3, self.f_kc.shape)
+        B = self.d_B
+        kv = self.d_ctx.cpu().tolist()
+        self.f_bytes = (sum(kv) * HKV * D * 1 * 2 + 2 * B * HQ * D * 2
+                        + 4 * sum(cdiv(k, BS) for k in kv))
+        self.f_reshape_bytes = 8 * B + 2 * B * HKV * D * 2 + 2 * B * HKV * D * 1
+
+    def decode_fp8_step(self):
+        capi = self.capi
+        st = capi.reshape_and_cache_ex(self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(),
+                                       self.d_slot.data_ptr(), self.f_kc.data_ptr(),
+                                       self.f_vc.data_ptr(), self.d_B, HKV, D, self.d_pool, BS,
+                                       capi.DATA_BFLOAT16, cache_dtype=capi.DATA_FLOAT8_E4M3,
+                                       k_scale=self.f_ks, v_scale=self.f_vs)
+        capi.check(st, "reshape_and_cache_ex fp8")
+
+    def decode_fp8_attn(self):
+        capi = self.capi
+        bt_d, q_d, _ = self.d_desc
+        st = capi.flash_attention_ex(self.h, 1, self.d_maxk, self.d_pool, self.d_ones.data_ptr(),
+                                     self.d_ctx.data_ptr(), bt_d, self.d_bt3.data_ptr(), q_d,
+                                     self.d_q3.data_ptr(), self.f_desc, self.f_kc.data_ptr(),
+                                     self.f_desc, self.f_vc.data_ptr(), q_d,
+                                     self.d_out3.data_ptr(), k_scale=self.f_ks,
+                                     v_scale=self.f_vs)
+        capi.check(st, "flash_attention_ex fp8")
+
     # ---- config 4: reshape sweep point (T = 65536, scattered, no padding)
     def setup_reshape(self, rank: int):
         torch = self.torch
@@ -374,6 +407,10 @@ def run_ours(args):
     dec_bytes_step = W.decode_bytes + W.decode_reshape_bytes
     (tf,) = timed_loop(torch, args.steps, args.warmup, [W.decode_fused])
     dec_fused_ms = max_over_ranks(sum(tf))
+    W.setup_decode_fp8()
+    fr, fa = timed_loop(torch, args.steps, args.warmup, [W.decode_fp8_step, W.decode_fp8_attn])
+    f_ms = max_over_ranks(sum(a + b for a, b in zip(fr, fa)))
+    f_attn_avg = sum(fa) / len(fa)
     decode = {
         "workload": "config 3: B=64 paged decode, ctx U{512..8192}+1, 40k-page pool, bs 16, bf16",
         "metric": "decode HBM GB/s", "unit": "GB/s",
@@ -387,8 +424,18 @@ def run_ours(args):
                          "one launch, same bytes)",
                   "ms_per_step": dec_fused_ms / args.steps,
                   "value": world * args.steps * dec_bytes_step / (dec_fused_ms * 1e-3) / 1e9},
+        "fp8_cache": {"api": "tecoopsReshapeAndCacheEx + tecoopsFlashAttentionEx, e4m3 cache "
+                             "(k/v scale 1/64), same shapes",
+                      "ms_per_step": f_ms / args.steps,
+                      "value": world * args.steps * (W.f_bytes + W.f_reshape_bytes)
+                      / (f_ms * 1e-3) / 1e9,
+                      "attn_kernel_us": f_attn_avg * 1e3,
+                      "attn_gbs": W.f_bytes / (f_attn_avg * 1e-3) / 1e9,
+                      "attn_frac_of_measured_hbm": W.f_bytes / (f_attn_avg * 1e-3) / 1e9
+                      / peaks["hbm_gbs"],
+                      "speedup_vs_bf16_step": (dec_ms / args.steps) / (f_ms / args.steps)},
     }
-    del W.d_kc, W.d_vc
+    del W.d_kc, W.d_vc, W.f_kc, W.f_vc
     torch.cuda.empty_cache()
     W.setup_reshape(rank)
     barrier()
@@ -612,6 +659,10 @@ def run_only(W, args, torch, rank):
     elif args.only == "decode":
         W.setup_decode(rank)
         ph, fl = [W.decode_step, W.decode_attn], None
+    elif args.only == "decode_fp8":
+        W.setup_decode(rank)
+        W.setup_decode_fp8()
+        ph, fl = [W.decode_fp8_step, W.decode_fp8_attn], None
     else:
         W.setup_reshape(rank)
         ph, fl = [W.reshape4], None
@@ -741,7 +792,7 @@ def main():
     ap.add_argument("--workload", choices=["config2", "70b"], default="config2",
                     help="config2 (default headline, weak scaling) or 70b (config 5, "
                          "KV-head sharded, strong scaling)")
-    ap.add_argument("--only", choices=["prefill", "decode", "reshape"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "decode_fp8", "reshape"], default=None,
                     help="run one workload's timed loop only (for profiler captures); "
                          "prints a reduced JSON line")
     args = ap.parse_args()

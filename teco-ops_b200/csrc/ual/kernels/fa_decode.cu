@@ -77,21 +77,18 @@ struct DecodeSmem {
     static constexpr int kBytes = (kUsed > kMergeBytes ? kUsed : kMergeBytes) + 1024;
 };
 
-// 16 e4m3 bytes -> 16 f16 (two 16-byte chunks), exact
+// 16 e4m3 bytes -> 16 f16 (two 16-byte chunks), exact: one cvt per byte pair
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t &o0, uint32_t &o1) {
+    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n"
+        " cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
+        : "=r"(o0), "=r"(o1)
+        : "r"(w));
+}
 __device__ __forceinline__ void e4m3x16_to_f16(const uint4 &in, uint4 &lo, uint4 &hi) {
-    const uint32_t w[4] = {in.x, in.y, in.z, in.w};
-    uint32_t o[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const __half2_raw a =
-            __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xffffu), __NV_E4M3);
-        const __half2_raw b =
-            __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
-        o[2 * i] = (uint32_t)a.x | ((uint32_t)a.y << 16);
-        o[2 * i + 1] = (uint32_t)b.x | ((uint32_t)b.y << 16);
-    }
-    lo = make_uint4(o[0], o[1], o[2], o[3]);
-    hi = make_uint4(o[4], o[5], o[6], o[7]);
+    e4m3x4_to_f16(in.x, lo.x, lo.y);
+    e4m3x4_to_f16(in.y, lo.z, lo.w);
+    e4m3x4_to_f16(in.z, hi.x, hi.y);
+    e4m3x4_to_f16(in.w, hi.z, hi.w);
 }
 
 // bf16x2 / f16x2 word -> f16x2 word

@@ -273,6 +273,26 @@ class Workloads:
             self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr())
         self.capi.check(st, "reshape_and_cache_flash_attention_decode")
 
+    # ---- rms_norm (the op before the QKV projection), residual form
+    def setup_rms(self):
+        torch = self.torch
+        self.n_T, hidden = 16 * self.tot, 4096
+        g = torch.Generator(device=self.dev).manual_seed(4000)
+        bf = torch.bfloat16
+        self.n_x = torch.randn(self.n_T, hidden, device=self.dev, dtype=bf, generator=g)
+        self.n_r = torch.randn(self.n_T, hidden, device=self.dev, dtype=bf, generator=g)
+        self.n_w = torch.randn(hidden, device=self.dev, dtype=bf, generator=g)
+        self.n_y = torch.empty_like(self.n_x)
+        self.n_ro = torch.empty_like(self.n_x)
+        self.n_bytes = self.n_T * hidden * 2 * 4 + hidden * 2   # x, r in; y, r_out out; w
+
+    def rms_step(self):
+        capi = self.capi
+        st = capi.rms_norm(self.h, self.n_x.data_ptr(), self.n_w.data_ptr(), self.n_r.data_ptr(),
+                           self.n_y.data_ptr(), self.n_ro.data_ptr(), self.n_T, 4096, 1e-6,
+                           dtype=capi.DATA_BFLOAT16)
+        capi.check(st, "rms_norm")
+
     # ---- config 3 on an e4m3 cache (extension): same shapes, half the cache bytes
     def setup_decode_fp8(self):
         torch, capi = self.torch, self.capi
@@ -441,6 +461,10 @@ def run_ours(args):
     barrier()
     (t4,) = timed_loop(torch, args.steps, args.warmup, [W.reshape4])
     r_ms = max_over_ranks(sum(t4))
+    del W.r_kc, W.r_vc
+    W.setup_rms()
+    (tn,) = timed_loop(torch, args.steps, args.warmup, [W.rms_step])
+    n_ms = max_over_ranks(sum(tn))
     clk = clocks.stop()   # sampled across every timed region above
     reshape = {
         "workload": "config 4: T=65536 scattered slots, 0% padding, 65536-page cache, bf16",
@@ -449,6 +473,15 @@ def run_ours(args):
         "kernel_us": r_ms / args.steps * 1e3,
         "frac_of_measured_hbm": W.r_bytes / (r_ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"],
         "l2": "inputs (537 MB) larger than L2",
+    }
+    rms = {
+        "workload": f"rms_norm with residual add, {W.n_T} tokens x hidden 4096 (Llama-3-8B "
+                    "layer input of config 2, 16 steps' worth), bf16",
+        "metric": "rms_norm HBM GB/s", "unit": "GB/s",
+        "value": world * args.steps * W.n_bytes / (n_ms * 1e-3) / 1e9,
+        "kernel_us": n_ms / args.steps * 1e3,
+        "frac_of_measured_hbm": W.n_bytes / (n_ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"],
+        "l2": f"inputs ({W.n_bytes / 1e6:.0f} MB) larger than L2",
     }
 
     cpu = None
@@ -478,6 +511,7 @@ def run_ours(args):
             "clocks": clk,
             "decode": decode,
             "reshape": reshape,
+            "rms_norm": rms,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu

@@ -318,6 +318,27 @@ tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(tecoopsHandle_t handle, int m
  */
 tecoopsStatus_t tecoopsGetDeviceErrorStatus(tecoopsHandle_t handle, int *error_code);
 
+/*
+ * rms_norm — RMSNorm, optionally fused with the residual add (the step before the
+ * QKV projection that feeds reshape_and_cache / flash_attention).
+ * Replaces reference tecoops.h rms_norm (teco/interface/ops/rms_norm.cpp).
+ *   input, output            : [num_tokens, hidden_size] fp16
+ *   weight                   : [hidden_size]
+ *   residual, residual_out   : [num_tokens, hidden_size] or nullptr (both or neither
+ *                              are used: residual_out = input + residual)
+ *   y = h * rstd * weight, rstd = 1 / sqrt(mean(h^2) + eps), h = input (+ residual)
+ * fp32 arithmetic; with a residual the sum of squares uses the unrounded h and the
+ * output the rounded residual_out, as the reference kernel does.
+ */
+tecoopsStatus_t tecoopsRmsNorm(tecoopsHandle_t handle, const void *input, const void *weight,
+                               const void *residual, void *output, void *residual_out,
+                               int num_tokens, int hidden_size, float eps);
+/* Extension: the same for TECOOPS_DATA_HALF or TECOOPS_DATA_BFLOAT16 tensors. */
+tecoopsStatus_t tecoopsRmsNormEx(tecoopsHandle_t handle, const void *input, const void *weight,
+                                 const void *residual, void *output, void *residual_out,
+                                 int num_tokens, int hidden_size, float eps,
+                                 tecoopsDataType_t dtype);
+
 /* ---- reference operators off this path: exported, NOT_SUPPORTED ---- */
 tecoopsStatus_t tecoopsFlattenRays(tecoopsHandle_t handle, const int *rays, uint32_t N,
                                    uint32_t M, int *res, tecoopsAlgo_t algo);
@@ -326,9 +347,6 @@ tecoopsStatus_t tecoopsReduceVariance(const tecoopsHandle_t handle, int axis, in
                                       const tecoopsTensorDescriptor_t yDesc, void *y);
 tecoopsStatus_t tecoopsMorton3DInvert(tecoopsHandle_t handle, const int *indices, uint32_t N,
                                       int *coords);
-tecoopsStatus_t tecoopsRmsNorm(tecoopsHandle_t handle, const void *input, const void *weight,
-                               const void *residual, void *output, void *residual_out,
-                               int num_tokens, int hidden_size, float eps);
 tecoopsStatus_t tecoopsCausalConv1d(tecoopsHandle_t handle, int batch, int totalSeqLen,
                                     int dim, int width, int convStateStride, int xSeqStride,
                                     int outSeqStride, int padSlotId, int api_mode, int actMode,

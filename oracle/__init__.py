@@ -9,6 +9,8 @@ package and ``libteco_ops.so``) never imports, links or calls anything here.
   test/zoo/teco/reshape_and_cache/reshape_and_cache.cpp:136-147.
 * :func:`flash_attn_varlen`: the torch golden
   test/zoo/teco/flash_attention/flash_attention.py:79-140 restated in numpy fp32.
+* :func:`rms_norm`: the zoo rms_norm golden, test/zoo/teco/rms_norm/rms_norm.cpp
+  (cpuCompute), restated in numpy fp32.
 * :mod:`oracle.fp8`: e4m3 encode / decode of the FP8 KV-cache extension (OCP E4M3
   definition; no reference counterpart).
 * :mod:`oracle.seeded`: deterministic counter-based input generator shared by
@@ -20,3 +22,4 @@ tests/test_oracle.py.
 """
 from .attention import flash_attn_varlen, attention_flops, attention_bytes  # noqa: F401
 from .reshape import reshape_and_cache, reshape_and_cache_np, reshape_bytes  # noqa: F401
+from .rms_norm import rms_norm, rms_norm_bytes  # noqa: F401

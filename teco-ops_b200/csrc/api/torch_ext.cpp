@@ -3,7 +3,8 @@
 // Drop-in for reference api/torch_ext.cpp:
 //   * pybind names kept: reshape_and_cache (61-79) and flash_attn_varlen_func
 //     (99-165, same 14 positional arguments) — torch_ext.cpp:208-215;
-//   * added, as the survey's north star asks: TORCH_LIBRARY(tecoops) ops
+//   * rms_norm (81-97), the adjacent operator of the same decoder layer;
+//   * added: TORCH_LIBRARY(tecoops) ops
 //     torch.ops.tecoops.reshape_and_cache / torch.ops.tecoops.flash_attention.
 // Differences from the reference binding (all B200-motivated):
 //   * q_seq_lens = diff(cu_seqlens_q) is computed ON THE DEVICE (the reference
@@ -111,6 +112,46 @@ void reshape_and_cache_torch(torch::Tensor key, torch::Tensor value, torch::Tens
                 "tecoopsReshapeAndCache");
 }
 
+// reference api/torch_ext.cpp:81-97: rms_norm(input, weight, residual, output,
+// residual_out, eps); fp16 through tecoopsRmsNorm, bf16 through tecoopsRmsNormEx
+void rms_norm_torch(torch::Tensor input, torch::Tensor weight,
+                    c10::optional<torch::Tensor> residual, torch::Tensor output,
+                    c10::optional<torch::Tensor> residual_out, double eps) {
+    checkCuda(input, "input");
+    checkCuda(weight, "weight");
+    checkCuda(output, "output");
+    TORCH_CHECK(input.dim() == 2 && input.is_contiguous() && output.is_contiguous(),
+                "input / output must be contiguous [num_tokens, hidden_size]");
+    TORCH_CHECK(output.sizes() == input.sizes(), "output must have the shape of input");
+    TORCH_CHECK(weight.numel() == input.size(1), "weight must be [hidden_size]");
+    const auto st = input.scalar_type();
+    TORCH_CHECK(st == at::kHalf || st == at::kBFloat16, "rms_norm: fp16 or bf16");
+    TORCH_CHECK(weight.scalar_type() == st && output.scalar_type() == st, "dtype mismatch");
+    const void *res = nullptr;
+    void *res_out = nullptr;
+    if (residual.has_value() && residual->defined()) {
+        TORCH_CHECK(residual_out.has_value() && residual_out->defined(),
+                    "residual_out is required with residual");
+        checkCuda(*residual, "residual");
+        checkCuda(*residual_out, "residual_out");
+        TORCH_CHECK(residual->sizes() == input.sizes() && residual_out->sizes() == input.sizes() &&
+                        residual->is_contiguous() && residual_out->is_contiguous(),
+                    "residual / residual_out must be contiguous like input");
+        TORCH_CHECK(residual->scalar_type() == st && residual_out->scalar_type() == st,
+                    "dtype mismatch");
+        res = residual->data_ptr();
+        res_out = residual_out->data_ptr();
+    }
+    if (input.size(0) == 0) return;
+    c10::cuda::CUDAGuard g(input.device());
+    tecoopsHandle_t h = handleFor(input.get_device());
+    checkStatus(tecoopsRmsNormEx(h, input.data_ptr(), weight.contiguous().data_ptr(), res,
+                                 output.data_ptr(), res_out, (int)input.size(0),
+                                 (int)input.size(1), (float)eps,
+                                 st == at::kBFloat16 ? TECOOPS_DATA_BFLOAT16 : TECOOPS_DATA_HALF),
+                "tecoopsRmsNorm");
+}
+
 static torch::Tensor run_flash(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                torch::Tensor q_lens, torch::Tensor kv_lens,
                                torch::Tensor block_table, int64_t max_seqlen_q,
@@ -191,7 +232,16 @@ void flash_attention_op(const at::Tensor &q, const at::Tensor &k_cache,
               block_table, max_seqlen_q, max_seqlen_k, out);
 }
 
+void rms_norm_op(const at::Tensor &input, const at::Tensor &weight,
+                 const c10::optional<at::Tensor> &residual, at::Tensor output,
+                 const c10::optional<at::Tensor> &residual_out, double eps) {
+    rms_norm_torch(input, weight, residual, output, residual_out, eps);
+}
+
 TORCH_LIBRARY(tecoops, m) {
+    m.def(
+        "rms_norm(Tensor input, Tensor weight, Tensor? residual, Tensor(a!) output, "
+        "Tensor(b!)? residual_out, float eps) -> ()");
     m.def(
         "reshape_and_cache(Tensor key, Tensor value, Tensor slot_mapping, Tensor(a!) key_cache, "
         "Tensor(b!) value_cache) -> ()");
@@ -204,10 +254,12 @@ TORCH_LIBRARY(tecoops, m) {
 TORCH_LIBRARY_IMPL(tecoops, CUDA, m) {
     m.impl("reshape_and_cache", &reshape_and_cache_op);
     m.impl("flash_attention", &flash_attention_op);
+    m.impl("rms_norm", &rms_norm_op);
 }
 
 PYBIND11_MODULE(_torch_ext, m) {
     m.def("reshape_and_cache", &reshape_and_cache_torch, "reshape_and_cache (sm_100a)");
+    m.def("rms_norm", &rms_norm_torch, "rms_norm (sm_100a)");
     m.def("flash_attn_varlen_func", &flash_attn_varlen_func_torch,
           "flash_attn_varlen_func (sm_100a)");
 }

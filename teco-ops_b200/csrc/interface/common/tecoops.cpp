@@ -236,10 +236,6 @@ tecoopsStatus_t tecoopsReduceVariance(const tecoopsHandle_t, int, int,
 tecoopsStatus_t tecoopsMorton3DInvert(tecoopsHandle_t, const int *, uint32_t, int *) {
     return TECOOPS_STATUS_NOT_SUPPORTED;
 }
-tecoopsStatus_t tecoopsRmsNorm(tecoopsHandle_t, const void *, const void *, const void *, void *,
-                               void *, int, int, float) {
-    return TECOOPS_STATUS_NOT_SUPPORTED;
-}
 tecoopsStatus_t tecoopsCausalConv1d(tecoopsHandle_t, int, int, int, int, int, int, int, int, int,
                                     int, const void *, void *, const void *, void *, const int *,
                                     const int *, const int8_t *) {

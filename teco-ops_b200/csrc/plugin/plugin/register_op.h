@@ -7,8 +7,9 @@
 //   * tvm::AttrsNode / TVM_DECLARE_ATTRS / TVM_ATTR_FIELD / TVM_REGISTER_NODE_TYPE
 //     (attribute declarations; values come from OpAttr / ComputeContext);
 //   * TECO_INFER::OpAttr::GetAttr<T>(name);
-//   * TECO_INFER::ComputeContext with GetInputDataPtr(name), GetOutputDataPtr(i),
-//     GetAttr(name, value), GetInputShape(name, shape) and GetStream();
+//   * TECO_INFER::ComputeContext with GetInputDataPtr(name or index),
+//     GetOutputDataPtr(i), GetAttr(name, value), GetInputShape(name or index, shape)
+//     and GetStream();
 //   * TECO_INFER::AbstractPluginOp with InferOutputShape and Enqueue;
 //   * REGISTER_PLUGIN_OP_IMPL(name, cls) and the PLUGIN_REGISTER_OP(name) spec
 //     builder (.Input/.Type/.Desc/.AttrType<>/.Register).
@@ -27,6 +28,7 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 // ---- TVM attribute declarations (declarative only in the stand-in) --------------
@@ -46,15 +48,19 @@ struct AttrFieldStub {
 
 namespace TECO_INFER {
 
-// Attribute values (all plugin attributes of this path are int64).
+// Attribute values: integer attributes (block sizes, dtypes) and floating ones (eps).
 class OpAttr {
  public:
     std::map<std::string, int64_t> ints;
+    std::map<std::string, double> floats;
     template <typename T>
     T GetAttr(const std::string &name) const {
+        auto f = floats.find(name);
         auto it = ints.find(name);
-        if (it == ints.end()) throw std::runtime_error("plugin attribute missing: " + name);
-        return static_cast<T>(it->second);
+        if (std::is_floating_point<T>::value && f != floats.end()) return static_cast<T>(f->second);
+        if (it != ints.end()) return static_cast<T>(it->second);
+        if (f != floats.end()) return static_cast<T>(f->second);
+        throw std::runtime_error("plugin attribute missing: " + name);
     }
 };
 
@@ -62,6 +68,7 @@ class ComputeContext {
  public:
     std::map<std::string, void *> inputs;
     std::map<std::string, std::vector<int>> shapes;
+    std::vector<std::string> input_order;   // inputs by position
     std::vector<void *> outputs;
     OpAttr attr;
     cudaStream_t stream = nullptr;
@@ -69,6 +76,15 @@ class ComputeContext {
     void *GetInputDataPtr(const std::string &name) {
         auto it = inputs.find(name);
         return it == inputs.end() ? nullptr : it->second;
+    }
+    void *GetInputDataPtr(int i) {
+        return i >= 0 && i < (int)input_order.size() ? GetInputDataPtr(input_order[i]) : nullptr;
+    }
+    void GetInputShape(int i, std::vector<int> &shape) {
+        if (i >= 0 && i < (int)input_order.size())
+            GetInputShape(input_order[i], shape);
+        else
+            shape.clear();
     }
     void *GetOutputDataPtr(int i) { return i < (int)outputs.size() ? outputs[i] : nullptr; }
     template <typename T>

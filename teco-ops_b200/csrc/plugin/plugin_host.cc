@@ -11,9 +11,13 @@
 namespace {
 std::string g_last_error;
 
-TECO_INFER::OpAttr make_attr(int n_attr, const char *const *names, const long long *vals) {
+// attribute values arrive as doubles: integral ones are stored as both kinds
+TECO_INFER::OpAttr make_attr(int n_attr, const char *const *names, const double *vals) {
     TECO_INFER::OpAttr a;
-    for (int i = 0; i < n_attr; ++i) a.ints[names[i]] = vals[i];
+    for (int i = 0; i < n_attr; ++i) {
+        a.floats[names[i]] = vals[i];
+        if (vals[i] == (double)(long long)vals[i]) a.ints[names[i]] = (long long)vals[i];
+    }
     return a;
 }
 
@@ -48,19 +52,22 @@ int teco_plugin_list(char *buf, int cap) {
     return (int)s.size();
 }
 
-// InferOutputShape of output 0: returns 0 and fills out_rank / out_dims (<= 8 dims).
+// InferOutputShape of n_out outputs: returns 0 and fills out_ranks[o] and
+// out_dims[8 * o + d] (<= 8 dims each).
 int teco_plugin_infer(const char *op, int n_in, const int *ranks, const int *dims_flat,
-                      int n_attr, const char *const *attr_names, const long long *attr_vals,
-                      int *out_rank, int *out_dims) {
+                      int n_attr, const char *const *attr_names, const double *attr_vals,
+                      int n_out, int *out_ranks, int *out_dims) {
     auto it = TECO_INFER::plugin_impls().find(op);
     if (it == TECO_INFER::plugin_impls().end()) return -1;
     try {
         auto impl = it->second();
-        std::vector<std::vector<int>> outs(1);
-        impl->InferOutputShape(make_shapes(n_in, ranks, dims_flat), n_in, outs, 1,
+        std::vector<std::vector<int>> outs(n_out);
+        impl->InferOutputShape(make_shapes(n_in, ranks, dims_flat), n_in, outs, n_out,
                                make_attr(n_attr, attr_names, attr_vals));
-        *out_rank = (int)outs[0].size();
-        for (int i = 0; i < *out_rank && i < 8; ++i) out_dims[i] = outs[0][i];
+        for (int o = 0; o < n_out; ++o) {
+            out_ranks[o] = (int)outs[o].size();
+            for (int i = 0; i < out_ranks[o] && i < 8; ++i) out_dims[8 * o + i] = outs[o][i];
+        }
         return 0;
     } catch (const std::exception &e) {
         g_last_error = e.what();
@@ -72,7 +79,7 @@ int teco_plugin_infer(const char *op, int n_in, const int *ranks, const int *dim
 int teco_plugin_enqueue(const char *op, int n_in, const char *const *in_names,
                         void *const *in_ptrs, const int *ranks, const int *dims_flat, int n_out,
                         void *const *out_ptrs, int n_attr, const char *const *attr_names,
-                        const long long *attr_vals, void *stream) {
+                        const double *attr_vals, void *stream) {
     auto it = TECO_INFER::plugin_impls().find(op);
     if (it == TECO_INFER::plugin_impls().end()) return -1;
     try {
@@ -81,6 +88,7 @@ int teco_plugin_enqueue(const char *op, int n_in, const char *const *in_names,
         for (int i = 0; i < n_in; ++i) {
             ctx->inputs[in_names[i]] = in_ptrs[i];
             ctx->shapes[in_names[i]] = shapes[i];
+            ctx->input_order.push_back(in_names[i]);
         }
         ctx->outputs.assign(out_ptrs, out_ptrs + n_out);
         ctx->attr = make_attr(n_attr, attr_names, attr_vals);

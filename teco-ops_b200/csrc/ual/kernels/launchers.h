@@ -10,6 +10,7 @@
 #include <cstdint>
 
 #include "ual/args/reshape_and_cache_args.h"
+#include "ual/args/rms_norm_args.h"
 
 namespace tecoops {
 namespace kern {
@@ -100,6 +101,9 @@ bool prefill_supported(int head_dim, int block_size, int group);
 size_t prefill_workspace_bytes(const AttnShape &s);
 cudaError_t launch_prefill(const AttnShape &s, bool bf16, void *workspace, int *dev_error,
                            int num_sms, cudaStream_t stream);
+
+// ---- rms_norm --------------------------------------------------------------------
+cudaError_t launch_rms_norm(const ual::args::RmsNormArgs &a, cudaStream_t stream);
 
 // ---- generic (any head_dim <= 256, any block_size) --------------------------------
 cudaError_t launch_generic_attention(const AttnShape &s, bool bf16, cudaStream_t stream);

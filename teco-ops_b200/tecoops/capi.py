@@ -33,7 +33,7 @@ EXPORTED = [
     "tecoopsReshapeAndCache", "tecoopsReshapeAndCacheEx", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
     "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlashAttentionEx",
     "tecoopsReshapeAndCacheFlashAttentionDecode", "tecoopsFlattenRays", "tecoopsReduceVariance",
-    "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsCausalConv1d",
+    "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsRmsNormEx", "tecoopsCausalConv1d",
 ]
 
 _vp = ctypes.c_void_p
@@ -98,6 +98,7 @@ def lib():
                                                        _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                                        _vp, _vp],
         "tecoopsRmsNorm": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float],
+        "tecoopsRmsNormEx": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_float, _i],
     }
     for name, args in sig.items():
         f = getattr(L, name)
@@ -230,6 +231,17 @@ def flash_attention_decode_noalloc(handle: Handle, max_seqlen_k, q_seq_lens, kv_
                                                     _vp(kv_seq_lens), bt_desc.d, _vp(block_table),
                                                     q_desc.d, _vp(q), k_desc.d, _vp(k_cache),
                                                     v_desc.d, _vp(v_cache), o_desc.d, _vp(out))
+
+
+def rms_norm(handle: Handle, input, weight, residual, output, residual_out, num_tokens,
+             hidden_size, eps, dtype=None) -> int:
+    """tecoopsRmsNorm (fp16) or, with dtype, tecoopsRmsNormEx; residual 0 = none."""
+    args = (handle.h, _vp(input), _vp(weight), _vp(residual) if residual else None, _vp(output),
+            _vp(residual_out) if residual_out else None, int(num_tokens), int(hidden_size),
+            float(eps))
+    if dtype is None:
+        return lib().tecoopsRmsNorm(*args)
+    return lib().tecoopsRmsNormEx(*args, int(dtype))
 
 
 def workspace_size(handle: Handle, max_seqlen_q, max_seqlen_k, bt_desc: Desc, q_desc: Desc,

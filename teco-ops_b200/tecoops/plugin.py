@@ -39,7 +39,7 @@ def registered() -> dict:
 
 def _attrs(attrs: dict):
     names = (ctypes.c_char_p * len(attrs))(*[k.encode() for k in attrs])
-    vals = (ctypes.c_longlong * len(attrs))(*[int(v) for v in attrs.values()])
+    vals = (ctypes.c_double * len(attrs))(*[float(v) for v in attrs.values()])
     return len(attrs), names, vals
 
 
@@ -50,16 +50,18 @@ def _shapes(shapes):
     return ranks, dims
 
 
-def infer_output_shape(op: str, input_shapes, attrs: dict):
+def infer_output_shape(op: str, input_shapes, attrs: dict, n_out: int = 1):
+    """Shape of output 0 (n_out == 1) or the list of the n_out output shapes."""
     ranks, dims = _shapes(input_shapes)
     na, names, vals = _attrs(attrs)
-    out_rank = ctypes.c_int()
-    out_dims = (ctypes.c_int * 8)()
+    out_ranks = (ctypes.c_int * n_out)()
+    out_dims = (ctypes.c_int * (8 * n_out))()
     st = lib().teco_plugin_infer(op.encode(), len(input_shapes), ranks, dims, na, names, vals,
-                                 ctypes.byref(out_rank), out_dims)
+                                 n_out, out_ranks, out_dims)
     if st != 0:
         raise RuntimeError(f"{op}: infer failed ({st}): {lib().teco_plugin_last_error().decode()}")
-    return list(out_dims)[:out_rank.value]
+    shapes = [list(out_dims)[8 * o:8 * o + out_ranks[o]] for o in range(n_out)]
+    return shapes[0] if n_out == 1 else shapes
 
 
 def enqueue(op: str, inputs: dict, outputs, attrs: dict, stream: int = 0):

@@ -206,3 +206,37 @@ def sample_index(n: int, k: int = 4096, seed: int = 7) -> np.ndarray:
     if n <= k:
         return np.arange(n, dtype=np.int64)
     return np.sort(seeded.permutation(seed + n, n)[:k])
+
+
+# ---------------------------------------------------------------- rms_norm
+# zoo test_case 0..7 (64 tokens, U(-1, 1) input / weight / residual) and
+# python_api_test/test_rms_norm.py (64 tokens, N(0, 1)), plus the B200 kernel
+# variants: bf16, ragged hidden sizes (scalar path), CTA-per-row sizes.
+def _rn(N, D, eps, res, dtype="f16", dist="uniform", seed=0):
+    return dict(N=N, D=D, eps=eps, res=res, dtype=dtype, dist=dist, seed=seed)
+
+
+RMS_CASES = {
+    "zoo0": _rn(64, 4096, 1e-6, False, seed=200), "zoo1": _rn(64, 4096, 1e-6, True, seed=201),
+    "zoo2": _rn(64, 2048, 1e-5, False, seed=202), "zoo3": _rn(64, 2048, 1e-5, True, seed=203),
+    "zoo4": _rn(64, 1536, 1e-6, False, seed=204), "zoo5": _rn(64, 1536, 1e-6, True, seed=205),
+    "zoo6": _rn(64, 128, 1e-6, False, seed=206), "zoo7": _rn(64, 128, 1e-5, False, seed=207),
+    "api_norm_128": _rn(64, 128, 1e-6, False, dist="normal", seed=210),
+    "api_add_4096": _rn(64, 4096, 1e-6, True, dist="normal", seed=211),
+    "bf16_add_8192": _rn(37, 8192, 1e-5, True, dtype="bf16", dist="normal", seed=212),
+    "bf16_norm_16384": _rn(5, 16384, 1e-6, False, dtype="bf16", dist="normal", seed=213),
+    "f16_ragged_100": _rn(9, 100, 1e-6, True, dist="normal", seed=214),
+    "f16_scalar_20000": _rn(3, 20000, 1e-5, False, dist="normal", seed=215),
+    "f16_one_token": _rn(1, 4096, 1e-6, True, dist="normal", seed=216),
+}
+
+
+def rms_inputs(c):
+    """(x, w, r or None) as 16-bit words."""
+    s = c["seed"]
+    gen = (lambda sd, shp: seeded.uniform(sd, shp, -1.0, 1.0)) if c["dist"] == "uniform" \
+        else seeded.normal
+    x = seeded.to_words(gen(s * 10 + 1, (c["N"], c["D"])), c["dtype"])
+    w = seeded.to_words(gen(s * 10 + 2, (c["D"],)), c["dtype"])
+    r = seeded.to_words(gen(s * 10 + 3, (c["N"], c["D"])), c["dtype"]) if c["res"] else None
+    return x, w, r

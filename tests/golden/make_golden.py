@@ -11,6 +11,8 @@ Goldens imported (three unavailable modules are stubbed in sys.modules):
   python_api_test/test_flash_attention.py (needs ``torch_sdaa``, ``tecoops``);
   inputs are converted exactly as test_flash_attention.py:167-181 does
   (16-bit -> fp32, cache permute [NB,H,bs,D] -> [NB,bs,H,D]).
+* rms_norm: ``rms_norm_ref`` / ``rms_norm_add_ref`` from
+  python_api_test/test_rms_norm.py (fp16 cases).
 * reshape_and_cache: ``reshape_and_cache_flash`` from
   python_api_test/test_reshape_and_cache.py on the vLLM-layout view, as that
   test does (sdaa_to_cpu permute).
@@ -61,8 +63,9 @@ def load_goldens(ref):
     import flash_attention as zoo_fa  # noqa: E402
     import test_flash_attention as api_fa  # noqa: E402
     import test_reshape_and_cache as api_rc  # noqa: E402
+    import test_rms_norm as api_rn  # noqa: E402
     return zoo_fa.flash_attn_varlen_func, api_fa.flash_attn_varlen_func_ref, \
-        api_rc.reshape_and_cache_flash
+        api_rc.reshape_and_cache_flash, (api_rn.rms_norm_ref, api_rn.rms_norm_add_ref)
 
 
 def words_to_torch_f32(w, dtype):
@@ -75,7 +78,7 @@ def words_to_torch16(w, dtype):
 
 
 def main(ref):
-    zoo_golden, api_golden, rc_golden = load_goldens(ref)
+    zoo_golden, api_golden, rc_golden, rn_golden = load_goldens(ref)
     torch.set_num_threads(os.cpu_count() or 1)
     out = {}
     for name, c in cases.ATTN_CASES.items():
@@ -114,7 +117,23 @@ def main(ref):
         out[f"rc/{name}/sha_k"] = np.frombuffer(hashlib.sha256(kres.tobytes()).digest(), np.uint8)
         out[f"rc/{name}/sha_v"] = np.frombuffer(hashlib.sha256(vres.tobytes()).digest(), np.uint8)
         print(f"reshape {name}: {int((slot >= 0).sum())} valid slots")
-    meta = {"attn": cases.ATTN_CASES, "rc": cases.RESHAPE_CASES,
+    for name, c in cases.RMS_CASES.items():
+        if c["dtype"] != "f16":
+            continue   # the reference golden is fp16 only
+        x, w, r = cases.rms_inputs(c)
+        xt, wt = words_to_torch16(x, "f16"), words_to_torch16(w, "f16")
+        if r is None:
+            outs = {"out": rn_golden[0](xt, wt, c["eps"])}
+        else:
+            o, ro = rn_golden[1](xt, words_to_torch16(r, "f16"), wt, c["eps"])
+            outs = {"out": o, "res_out": ro}
+        for key, t in outs.items():
+            flat = t.float().numpy().reshape(-1)
+            idx = cases.sample_index(flat.size)
+            out[f"rms/{name}/{key}/idx"] = idx
+            out[f"rms/{name}/{key}/val"] = flat[idx]
+        print(f"rms_norm {name}: {tuple(xt.shape)} residual={r is not None}")
+    meta = {"attn": cases.ATTN_CASES, "rc": cases.RESHAPE_CASES, "rms": cases.RMS_CASES,
             "generator": "tests/golden/make_golden.py", "torch": torch.__version__}
     out["meta"] = np.frombuffer(json.dumps(meta, sort_keys=True).encode(), np.uint8)
     path = os.path.join(HERE, "golden.npz")

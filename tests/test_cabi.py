@@ -149,9 +149,23 @@ def test_workspace_query():
     assert capi.workspace_size(h, 128, 8192, bt, q, k) == 0
 
 
+def test_rms_norm_host_checks():
+    """reference teco/interface/ops/rms_norm.cpp checkRmsNormInput."""
+    L = capi.lib()
+    h = capi.Handle()
+    p = ctypes.c_void_p(16)
+    assert L.tecoopsRmsNorm(None, p, p, None, p, None, 1, 1, 1e-6) == capi.NOT_INITIALIZED
+    assert L.tecoopsRmsNorm(h.h, None, p, None, p, None, 1, 1, 1e-6) == capi.BAD_PARAM
+    assert L.tecoopsRmsNorm(h.h, p, p, None, None, None, 1, 1, 1e-6) == capi.BAD_PARAM
+    assert L.tecoopsRmsNorm(h.h, p, p, p, p, None, 1, 1, 1e-6) == capi.BAD_PARAM   # no residual_out
+    assert L.tecoopsRmsNorm(h.h, p, p, None, p, None, 0, 8, 1e-6) == capi.BAD_PARAM
+    assert L.tecoopsRmsNorm(h.h, p, p, None, p, None, 4, 0, 1e-6) == capi.BAD_PARAM
+    assert L.tecoopsRmsNormEx(h.h, p, p, None, p, None, 4, 8, 1e-6, capi.DATA_FLOAT) == \
+        capi.BAD_PARAM
+
+
 def test_off_path_ops_not_supported():
     L = capi.lib()
     h = capi.Handle()
-    assert L.tecoopsRmsNorm(h.h, None, None, None, None, None, 1, 1, 1e-6) == capi.NOT_SUPPORTED
     assert L.tecoopsMemset(None, None, 0, 0) == capi.NOT_INITIALIZED
     assert L.tecoopsMemset(h.h, None, 0, 16) == capi.BAD_PARAM

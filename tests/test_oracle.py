@@ -15,6 +15,7 @@ def test_fixture_meta_matches_cases(golden):
     meta = json.loads(bytes(golden["meta"]).decode())
     assert meta["attn"] == json.loads(json.dumps(cases.ATTN_CASES))
     assert meta["rc"] == json.loads(json.dumps(cases.RESHAPE_CASES))
+    assert meta["rms"] == json.loads(json.dumps(cases.RMS_CASES))
 
 
 @pytest.mark.parametrize("name", sorted(cases.ATTN_CASES))
@@ -159,3 +160,30 @@ def test_fp8_oracle_matches_torch_e4m3():
     ok = ~np.isnan(fp8.decode(codes))
     assert np.array_equal(fp8.encode(fp8.decode(codes))[ok], codes[ok] & np.where(
         codes[ok] == 0x80, 0xFF, 0xFF).astype(np.uint8))
+
+
+def _half_ulp(v):
+    """Spacing of fp16 at |v| (normal range; 2^-24 in the subnormal range)."""
+    a = np.maximum(np.abs(v.astype(np.float32)), np.float32(2.0 ** -14))
+    return np.exp2(np.floor(np.log2(a)) - 10)
+
+
+@pytest.mark.parametrize("name", sorted(cases.RMS_CASES))
+def test_rms_norm_oracle_vs_reference_golden(golden, name):
+    """The numpy restatement of the zoo golden against the reference's python
+    golden: residual_out bit-exact, output within one fp16 step (the python golden
+    multiplies the unrounded residual sum; the zoo golden, the kernel and the
+    oracle the rounded one; reduction order also differs)."""
+    c = cases.RMS_CASES[name]
+    if c["dtype"] != "f16":
+        pytest.skip("the reference golden is fp16 only")
+    x, w, r = cases.rms_inputs(c)
+    y, ro = oracle.rms_norm(x, w, r, c["eps"], "f16")
+    yf = seeded.words_to_f32(y, "f16").reshape(-1)
+    idx = golden[f"rms/{name}/out/idx"]
+    g = golden[f"rms/{name}/out/val"]
+    assert np.all(np.abs(yf[idx] - g) <= _half_ulp(g) * (2 if r is not None else 1) + 1e-7)
+    if r is not None:
+        rf = seeded.words_to_f32(ro, "f16").reshape(-1)
+        ridx = golden[f"rms/{name}/res_out/idx"]
+        assert np.array_equal(rf[ridx], golden[f"rms/{name}/res_out/val"])

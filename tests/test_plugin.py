@@ -33,3 +33,15 @@ def test_unknown_plugin_and_missing_attribute():
     with pytest.raises(RuntimeError):
         plugin.infer_output_shape("plugin_reshape_and_cache", [[4, 2, 8], [4, 2, 8], [4]],
                                   {"num_blocks": 4})
+
+
+def test_rms_norm_plugins_registered_and_shapes():
+    """plugin_rms_norm / plugin_rms_norm_add (reference
+    teco/plugin/pluginRmsNorm/plugin_rms_norm.cc): outputs shaped like the input."""
+    reg = plugin.registered()
+    assert reg["plugin_rms_norm"] == ["input", "weight"]
+    assert reg["plugin_rms_norm_add"] == ["input", "weight", "residual"]
+    assert plugin.infer_output_shape("plugin_rms_norm", [[64, 4096], [4096]],
+                                     {"eps": 1e-6}) == [64, 4096]
+    assert plugin.infer_output_shape("plugin_rms_norm_add", [[7, 128], [128], [7, 128]],
+                                     {"eps": 1e-5}, n_out=2) == [[7, 128], [7, 128]]

@@ -28,8 +28,7 @@
 //   warps 2-5   softmax of sub-tile 0, warps 6-9 of sub-tile 1: thread r owns
 //               row r = TMEM lane r (r = 32*(warp%4) + lane); the 128-score row is
 //               read from TMEM in one burst, max by 3-input max trees, exp2 on the
-//               MUFU unit for 10 of every 16 pairs and by a fitted polynomial on the
-//               FMA pipe for the rest (packed f32x2 arithmetic), 16-bit P written over
+//               MUFU unit (scale and sums in packed f32x2 arithmetic), 16-bit P written over
 //               the S columns it came from, lazy O rescale (only when the running max
 //               grows by more than 2^8), epilogue O / l -> global.
 // TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,256+D) O_1 [384,384+D).
@@ -155,33 +154,6 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&u)[32], int lo, int 
     return fmax3(m[0], fmax3(m[1], m[2], m[3]), -INFINITY);
 }
 
-// 2^x for a pair of finite x on the FMA/ALU pipes, to take load off the MUFU unit:
-// x = n + f with n = rint(x) (via the 1.5*2^23 rounding constant) and f in [-0.5, 0.5];
-// 2^f by a degree-3 polynomial 1 + f(c1 + f(c2 + f c3)) fitted here for minimum
-// relative error on [-0.5, 0.5] (max relative error 1.0e-4, far below the 2^-8
-// resolution of the 16-bit P it feeds); 2^n is added into the exponent field.
-// x is clamped at -125 (the result is then ~2e-38, i.e. zero for P; the exponent
-// field of p (126 or 127) minus 125 stays positive).
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float &y1) {
-    constexpr float kRound = 12582912.f;   // 1.5 * 2^23
-    x0 = fmaxf(x0, -125.f);
-    x1 = fmaxf(x1, -125.f);
-    const uint64_t x2 = f2pack(x0, x1);
-    const uint64_t t2 = fadd2(x2, f2pack(kRound, kRound));          // round(x) in low bits
-    const uint64_t r2 = fadd2(t2, f2pack(-kRound, -kRound));        // round(x) as float
-    const uint64_t fr = ffma2(r2, f2pack(-1.f, -1.f), x2);          // f = x - round(x)
-    uint64_t pp = ffma2(fr, f2pack(0.05500892922282219f, 0.05500892922282219f),
-                        f2pack(0.2422109693288803f, 0.2422109693288803f));
-    pp = ffma2(pp, fr, f2pack(0.6932829022407532f, 0.6932829022407532f));
-    pp = ffma2(pp, fr, f2pack(1.f, 1.f));
-    float p0, p1, t0, t1;
-    f2unpack(pp, p0, p1);
-    f2unpack(t2, t0, t1);
-    // low bits of t hold round(x) (two's complement); << 23 moves it into the exponent
-    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
 // p = 2^(s*scale - m) for 32 scores, packed to 16-bit pairs; row sum accumulated
 // in two packed fp32 accumulators
 template <typename T, bool MASKED>
@@ -197,15 +169,11 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&u)[32], int lo, int n
             x0 = (unsigned)(e - lo) < w ? x0 : -INFINITY;
             x1 = (unsigned)(e + 1 - lo) < w ? x1 : -INFINITY;
         }
-        float t0, t1, p0, p1;
+        float t0, t1;
         f2unpack(ffma2(f2pack(x0, x1), sl2x2, negm2), t0, t1);
-        // unmasked tiles: 6 of every 16 pairs on the FMA pipe, the rest on MUFU
-        if (!MASKED && ((e >> 1) & 7) >= 5) {
-            exp2_poly2(t0, t1, p0, p1);
-        } else {
-            p0 = fast_exp2(t0);
-            p1 = fast_exp2(t1);
-        }
+        // every exp2 on the MUFU unit: moving a share of them to a polynomial on the
+        // FMA pipe measured slower here (the softmax chain is latency-bound)
+        const float p0 = fast_exp2(t0), p1 = fast_exp2(t1);
         sum[(e >> 1) & 1] = fadd2(sum[(e >> 1) & 1], f2pack(p0, p1));
         pk[e >> 1] = Elem<T>::pack2(p0, p1);
     }

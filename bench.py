@@ -693,6 +693,9 @@ def run_only(W, args, torch, rank):
     elif args.only == "decode":
         W.setup_decode(rank)
         ph, fl = [W.decode_step, W.decode_attn], None
+    elif args.only == "rms_norm":
+        W.setup_rms()
+        ph, fl = [W.rms_step], None
     elif args.only == "decode_fp8":
         W.setup_decode(rank)
         W.setup_decode_fp8()
@@ -826,7 +829,7 @@ def main():
     ap.add_argument("--workload", choices=["config2", "70b"], default="config2",
                     help="config2 (default headline, weak scaling) or 70b (config 5, "
                          "KV-head sharded, strong scaling)")
-    ap.add_argument("--only", choices=["prefill", "decode", "decode_fp8", "reshape"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "decode_fp8", "reshape", "rms_norm"], default=None,
                     help="run one workload's timed loop only (for profiler captures); "
                          "prints a reduced JSON line")
     args = ap.parse_args()

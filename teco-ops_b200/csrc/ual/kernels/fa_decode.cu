@@ -517,10 +517,14 @@ void decode_plan(int num_sms, int batch, int kv_heads, int group, int max_k, int
                  int *max_splits) {
     const int slices = (group + 15) / 16;
     const int64_t work = (int64_t)batch * kv_heads * slices * (int64_t)(max_k > 0 ? max_k : 1);
-    const int64_t target = (int64_t)num_sms * 2 * 8;   // ~8 waves of 2 CTAs per SM
+    // Many short CTAs even out the tail (splits end at different kv_len), but each CTA
+    // pays a start-up and adds a merge record: ~64 waves of 2 CTAs per SM with at least
+    // 1536 tokens per split measured best on both the B=64 (ctx <= 8k) and the B=256
+    // (ctx <= 32k) decode workloads (8 waves / 256 tokens left 10 % on the table at B=256).
+    const int64_t target = (int64_t)num_sms * 2 * 64;
     int64_t split = (work + target - 1) / target;
     split = ((split + 63) / 64) * 64;
-    if (split < 256) split = 256;
+    if (split < 1536) split = 1536;
     const int64_t cap = ((int64_t)(max_k > 0 ? max_k : 1) + 63) / 64 * 64;
     if (split > cap) split = cap < 64 ? 64 : cap;
     *split_tokens = (int)split;

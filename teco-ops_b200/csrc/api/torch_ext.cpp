@@ -9,9 +9,8 @@
 // Differences from the reference binding (all B200-motivated):
 //   * q_seq_lens = diff(cu_seqlens_q) is computed ON THE DEVICE (the reference
 //     copies cu_seqlens_q to the host and back, a sync per call, 118-126);
-//   * one handle per (host thread, device); its stream is set to PyTorch's
-//     current CUDA stream on every call (the reference uses one global handle on
-//     the default stream, 35-42);
+//   * one handle per (host thread, device, PyTorch stream), bound to that stream
+//     (the reference uses one global handle on the default stream, 35-42);
 //   * dtypes fp16 and bf16 (the reference hard-codes HALF descriptors);
 //   * `out` is not zero-filled first: every row inside a sequence is written,
 //     rows past sum(q_lens) are left untouched; an undefined/empty `out` is
@@ -28,23 +27,30 @@
 #include <torch/library.h>
 
 #include <array>
+#include <map>
+#include <utility>
 #include <vector>
 
 #include "tecoops.h"
 
 namespace {
 
+// One handle per (host thread, device, CUDA stream): a handle owns device scratch
+// (split-KV partials, the prefill unit scheduler's counters) that concurrent launches
+// on different streams must not share -- the reference's rule of one handle per
+// thread or stream, kept for callers that switch PyTorch streams.
 tecoopsHandle_t handleFor(int device) {
-    thread_local std::array<tecoopsHandle_t, 64> handles{};
-    TORCH_CHECK(device >= 0 && device < 64, "tecoops: device index out of range");
-    if (handles[device] == nullptr) {
+    thread_local std::map<std::pair<int, cudaStream_t>, tecoopsHandle_t> handles;
+    TORCH_CHECK(device >= 0, "tecoops: device index out of range");
+    const cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
+    tecoopsHandle_t &h = handles[{device, stream}];
+    if (h == nullptr) {
         c10::cuda::CUDAGuard g(device);
-        tecoopsStatus_t st = tecoopsCreate(&handles[device]);
+        tecoopsStatus_t st = tecoopsCreate(&h);
         TORCH_CHECK(st == TECOOPS_STATUS_SUCCESS, "tecoopsCreate failed: ",
                     tecoopsGetErrorString(st));
+        tecoopsSetStream(h, stream);
     }
-    tecoopsHandle_t h = handles[device];
-    tecoopsSetStream(h, at::cuda::getCurrentCUDAStream(device).stream());
     return h;
 }
 

@@ -122,3 +122,34 @@ def test_binding_rejects_cpu_tensors():
                                   torch.zeros(1, dtype=torch.long),
                                   torch.zeros(1, 1, 16, 8, dtype=torch.half),
                                   torch.zeros(1, 1, 16, 8, dtype=torch.half))
+
+
+def test_binding_two_streams_concurrently():
+    """Prefill and decode launched on two PyTorch streams at once from one thread:
+    each (thread, device, stream) gets its own handle, so the split-KV scratch and the
+    prefill scheduler's counters are not shared; results equal the serial ones."""
+    import tecoops
+    from gpu_util import attn_case_to_dev
+    outs = {}
+    runs = []
+    for name in ("bf16_bs16_varlen", "bf16_bs16_decode"):
+        c = cases.ATTN_CASES[name]
+        inp = cases.attn_inputs(c)
+        d = attn_case_to_dev(inp, c["dtype"])
+        ql = inp["q_lens"]
+        cu = torch.zeros(len(ql) + 1, dtype=torch.int32)
+        cu[1:] = torch.from_numpy(np.cumsum(ql)).to(torch.int32)
+        args = (d["q"], d["kc"], d["vc"], int(ql.max()), cu.cuda(), int(inp["kv_lens"].max()),
+                torch.Tensor(), d["kv_lens"], 0.0, True, torch.Tensor(), d["bt"], False)
+        ref = tecoops.flash_attn_varlen_func(*args, torch.empty_like(d["q"]))
+        torch.cuda.synchronize()
+        runs.append((name, args, ref))
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for it in range(5):
+        for (name, args, _), st in zip(runs, streams):
+            with torch.cuda.stream(st):
+                outs[(name, it)] = tecoops.flash_attn_varlen_func(*args, torch.empty_like(args[0]))
+    torch.cuda.synchronize()
+    for name, _, ref in runs:
+        for it in range(5):
+            assert torch.equal(outs[(name, it)], ref), (name, it)

@@ -102,6 +102,31 @@ size_t prefill_workspace_bytes(const AttnShape &s);
 cudaError_t launch_prefill(const AttnShape &s, bool bf16, void *workspace, int *dev_error,
                            int num_sms, cudaStream_t stream);
 
+// ---- e4m3 cache -> 16-bit compact cache for the tcgen05 prefill ------------------
+struct KvDequantParams {
+    const void *key_cache;     // e4m3, layout kv_layout
+    const void *value_cache;
+    const int *kv_seq_lens;
+    const int *block_table;    // [batch, block_table_dim]
+    void *key_out;             // 16-bit [batch * pages_per_seq, Hkv, block_size, D]
+    void *value_out;
+    int *bt_out;               // [batch, pages_per_seq]: b * pages_per_seq + i
+    int batch;
+    int pages_per_seq;         // ceil(max_seqlen_k / block_size)
+    int block_table_dim;
+    int num_pages;
+    int num_kv_heads;
+    int block_size;
+    int head_dim;
+    int kv_layout;
+    float k_scale;
+    float v_scale;
+};
+size_t kv_dequant_workspace_bytes(int batch, int pages_per_seq, int num_kv_heads, int block_size,
+                                  int head_dim);
+cudaError_t launch_kv_dequant(const KvDequantParams &p, bool bf16, int num_sms,
+                              cudaStream_t stream);
+
 // ---- rms_norm --------------------------------------------------------------------
 cudaError_t launch_rms_norm(const ual::args::RmsNormArgs &a, cudaStream_t stream);
 

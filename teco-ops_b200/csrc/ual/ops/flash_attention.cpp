@@ -3,6 +3,7 @@
 #include "ual/ops/flash_attention.hpp"
 
 #include <cmath>
+#include <cstdint>
 
 #include "ual/kernels/launchers.h"
 
@@ -93,9 +94,52 @@ static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
     return kern::launch_decode(p, a.dtype == ElemType::BF16, stream);
 }
 
+static int pagesPerSeq(const FlashAttentionArgs &a) {
+    return (a.max_k_seq_len + a.block_size - 1) / a.block_size;
+}
+
+// e4m3 cache: its referenced pages are dequantised into a compact 16-bit cache in the
+// workspace first (kern::launch_kv_dequant), then the tcgen05 prefill runs on that
 static cudaError_t runPrefill(const FlashAttentionArgs &a, cudaStream_t stream) {
-    return kern::launch_prefill(toShape(a), a.dtype == ElemType::BF16, a.workspace, a.dev_error,
-                                a.num_sms, stream);
+    const bool bf16 = a.dtype == ElemType::BF16;
+    kern::AttnShape s = toShape(a);
+    if (a.cache_fp8) {
+        kern::KvDequantParams d;
+        d.key_cache = a.key_cache;
+        d.value_cache = a.value_cache;
+        d.kv_seq_lens = a.kv_seq_lens;
+        d.block_table = a.block_table;
+        d.batch = a.batch_size;
+        d.pages_per_seq = pagesPerSeq(a);
+        d.block_table_dim = a.block_table_dim;
+        d.num_pages = a.max_block_num;
+        d.num_kv_heads = a.local_kv_head_num;
+        d.block_size = a.block_size;
+        d.head_dim = a.size_per_head;
+        d.kv_layout = a.kv_layout;
+        d.k_scale = a.k_scale;
+        d.v_scale = a.v_scale;
+        const size_t need = kern::kv_dequant_workspace_bytes(d.batch, d.pages_per_seq,
+                                                             d.num_kv_heads, d.block_size,
+                                                             d.head_dim);
+        if (a.workspace == nullptr || a.workspace_bytes < need) return cudaErrorInvalidValue;
+        const size_t cache = (size_t)d.batch * d.pages_per_seq * d.num_kv_heads * d.block_size *
+                             d.head_dim * 2;
+        uint8_t *base = static_cast<uint8_t *>(a.workspace);
+        d.key_out = base;
+        d.value_out = base + cache;
+        d.bt_out = reinterpret_cast<int *>(base + 2 * cache);
+        cudaError_t e = kern::launch_kv_dequant(d, bf16, a.num_sms, stream);
+        if (e != cudaSuccess) return e;
+        s.key_cache = d.key_out;
+        s.value_cache = d.value_out;
+        s.block_table = d.bt_out;
+        s.block_table_dim = d.pages_per_seq;
+        s.num_pages = d.batch * d.pages_per_seq;
+        s.kv_layout = 0;
+        s.cache_fp8 = 0;
+    }
+    return kern::launch_prefill(s, bf16, nullptr, a.dev_error, a.num_sms, stream);
 }
 
 static cudaError_t runGeneric(const FlashAttentionArgs &a, cudaStream_t stream) {
@@ -106,8 +150,8 @@ FlashAttentionAlgos FlashAttentionOp::selectAlgo(const FlashAttentionArgs &a) {
     const int group = a.local_head_num / a.local_kv_head_num;
     if (a.max_q_seq_len == 1 && kern::decode_supported(a.size_per_head, a.block_size, group))
         return FlashAttentionAlgos::DECODE_SPLITKV;
-    // the tcgen05 prefill reads 16-bit caches only; e4m3 caches prefill generically
-    if (!a.cache_fp8 && kern::prefill_supported(a.size_per_head, a.block_size, group))
+    // e4m3 caches reach the tcgen05 prefill through a dequantised compact copy
+    if (kern::prefill_supported(a.size_per_head, a.block_size, group))
         return FlashAttentionAlgos::PREFILL_TCGEN05;
     return FlashAttentionAlgos::GENERIC;
 }
@@ -121,6 +165,10 @@ size_t FlashAttentionOp::workspaceSize(const FlashAttentionArgs &a) {
                                                 ms);
         }
         case FlashAttentionAlgos::PREFILL_TCGEN05:
+            if (a.cache_fp8)
+                return kern::kv_dequant_workspace_bytes(a.batch_size, pagesPerSeq(a),
+                                                        a.local_kv_head_num, a.block_size,
+                                                        a.size_per_head);
             return kern::prefill_workspace_bytes(toShape(a));
         default:
             return 0;

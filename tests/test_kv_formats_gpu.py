@@ -132,7 +132,8 @@ def test_attention_vllm_layout_matches_reference_layout(name):
                                          ("bf16_bs16_varlen", 1), ("bf16_d64_bs64", 0)])
 def test_attention_fp8_cache_vs_oracle(name, layout):
     """e4m3 caches: decode on the split-KV kernel (f16 MMAs on converted tiles),
-    prefill and odd shapes on the generic kernel."""
+    prefill on the tcgen05 kernel over a dequantised compact copy, odd shapes on the
+    generic kernel."""
     from gpu_util import errors, words_to_dev
     from tecoops import capi
     c = cases.ATTN_CASES[name]
@@ -195,5 +196,33 @@ def test_fp8_vllm_decode_step_round_trip():
     vhnd = fp8.dequantize(vc.cpu().numpy(), vs).transpose(0, 2, 1, 3)
     ref = oracle.flash_attn_varlen(q.float().cpu().numpy(), khnd, vhnd, [1] * B,
                                    (ctx + 1).tolist(), bt.numpy())
+    mx, mean, diff1 = errors(out.float().cpu().numpy(), ref)
+    assert mx <= 2e-2 and mean <= 2e-3 and diff1 <= 1e-2, (mx, mean, diff1)
+
+
+def test_fp8_prefill_config2_full_size():
+    """BASELINE config 2 shapes on an e4m3 cache (scale 1/64) through the tcgen05
+    prefill: tolerance against the oracle on the dequantised cache."""
+    from gpu_util import errors
+    from tecoops import capi
+    lens = torch.randint(512, 2049, (4,), generator=torch.Generator().manual_seed(10)).tolist()
+    Hq, Hkv, D, bs, ks, vs = 32, 8, 128, 16, 1.0 / 64, 1.0 / 64
+    pages = [(l + bs - 1) // bs for l in lens]
+    NB = sum(pages)
+    bt = torch.zeros(4, max(pages), dtype=torch.int32)
+    p0 = 0
+    for b in range(4):
+        bt[b, :pages[b]] = torch.arange(p0, p0 + pages[b], dtype=torch.int32)
+        p0 += pages[b]
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q = torch.randn(sum(lens), Hq, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    kc = (torch.randn(NB, Hkv, bs, D, device="cuda", generator=g) / ks).to(
+        torch.float8_e4m3fn).view(torch.uint8)
+    vc = (torch.randn(NB, Hkv, bs, D, device="cuda", generator=g) / vs).to(
+        torch.float8_e4m3fn).view(torch.uint8)
+    ql = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = _attn_ex(q, kc, vc, ql, ql, bt.cuda(), capi.DATA_FLOAT8_E4M3, k_scale=ks, v_scale=vs)
+    ref = oracle.flash_attn_varlen(q.float().cpu().numpy(), fp8.dequantize(kc.cpu().numpy(), ks),
+                                   fp8.dequantize(vc.cpu().numpy(), vs), lens, lens, bt.numpy())
     mx, mean, diff1 = errors(out.float().cpu().numpy(), ref)
     assert mx <= 2e-2 and mean <= 2e-3 and diff1 <= 1e-2, (mx, mean, diff1)

@@ -116,13 +116,6 @@ __device__ __forceinline__ int warp_seq_start(const int *__restrict__ lens, int 
     return acc;
 }
 
-// Same as warp_seq_start for a single thread (no warp cooperation needed).
-__device__ __forceinline__ int warp_seq_start_lane0(const int *__restrict__ lens, int b) {
-    int acc = 0;
-    for (int i = 0; i < b; ++i) acc += __ldg(lens + i);
-    return acc;
-}
-
 }  // namespace kern
 }  // namespace tecoops
 

@@ -105,7 +105,15 @@ struct PrefillParams {
     int window_left;    //   j <= off + i (causal) / off + i + window_right (non-causal,
     int window_right;   //   right >= 0); j >= off + i - window_left (left >= 0)
     float *lse;         // optional [Hq, total_q] natural-log log-sum-exp
+    int out_al32;       // out is 32-byte aligned: rows are written with 256-bit stores
 };
+
+// eight 32-bit words to a 32-byte aligned global address in one instruction
+__device__ __forceinline__ void st_global_v8(void *ptr, const uint32_t *w) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"l"(ptr), "r"(w[0]),
+                 "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+}
 
 #ifdef TECOOPS_PREFILL_TRACE
 // Development-only timeline capture (not built into the library): per CTA, clock64()
@@ -730,11 +738,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int e = 0; e < 16; ++e)
                         pkd[e] = Elem<T>::pack2(__uint_as_float(ov[c][2 * e]) * inv,
                                                 __uint_as_float(ov[c][2 * e + 1]) * inv);
-                    uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
+                    if (p.out_al32) {
+                        // 256-bit stores: each covers one whole 32-byte sector of the row
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        dst[e] = make_uint4(pkd[4 * e], pkd[4 * e + 1], pkd[4 * e + 2],
-                                            pkd[4 * e + 3]);
+                        for (int e = 0; e < 2; ++e)
+                            st_global_v8(orow + c * 32 + 16 * e, &pkd[8 * e]);
+                    } else {
+                        uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            dst[e] = make_uint4(pkd[4 * e], pkd[4 * e + 1], pkd[4 * e + 2],
+                                                pkd[4 * e + 3]);
+                    }
                 }
             }
             if (warp == 2 && lane == 0) UTRACE(ocount - 1, 5, clock64());
@@ -830,6 +845,7 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, int num_
     p.window_left = s.window_left;
     p.window_right = s.window_right;
     p.lse = s.lse;
+    p.out_al32 = (reinterpret_cast<uintptr_t>(s.out) & 31u) == 0 ? 1 : 0;
     if (p.num_units <= 0 || s.batch <= 0) return cudaSuccess;
 
     auto kfn = s.window_left >= 0 ? fa_prefill_sm100_kernel<T, D, true>

@@ -476,10 +476,16 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
 
 // Combine the split partials of every (sequence, q head) that used more than
 // one split: out = sum_s 2^(lse_s - M) O_s / sum_s 2^(lse_s - M).
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
-    const int b = blockIdx.x / p.num_heads;
-    const int h = blockIdx.x - b * p.num_heads;
+    // one warp per (sequence, q head): lanes read the split log2-sum-exps in parallel,
+    // reduce by shuffle, and each lane accumulates D/32 consecutive output columns
+    constexpr int kPer = D / 32;
+    const int lane = threadIdx.x & 31;
+    const int rec_id = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (rec_id >= p.batch * p.num_heads) return;
+    const int b = rec_id / p.num_heads;
+    const int h = rec_id - b * p.num_heads;
     const int q_len = __ldg(p.q_seq_lens + b);
     const int kv_len = __ldg(p.kv_seq_lens + b);
     const int kv_lo = p.window_left >= 0 ? max(0, kv_len - 1 - p.window_left) : 0;
@@ -489,21 +495,40 @@ __global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
     if (qrow >= p.total_q) return;
     const int64_t rec0 = ((int64_t)b * p.num_heads + h) * p.max_splits;
     float M = -INFINITY;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, p.part_lse[rec0 + s]);
+    for (int sp = lane; sp < ns; sp += 32) M = fmaxf(M, p.part_lse[rec0 + sp]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float Mu = M == -INFINITY ? 0.f : M;
-    for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
-        float W = 0.f, O = 0.f;
-        for (int s = 0; s < ns; ++s) {
-            const float w = fast_exp2(p.part_lse[rec0 + s] - Mu);
+    float W = 0.f, O[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) O[i] = 0.f;
+    for (int s0 = 0; s0 < ns; s0 += 32) {
+        const int sp = s0 + lane;
+        const float wl = sp < ns ? fast_exp2(p.part_lse[rec0 + sp] - Mu) : 0.f;
+        const int cnt = min(32, ns - s0);
+        for (int t = 0; t < cnt; ++t) {
+            const float w = __shfl_sync(0xffffffffu, wl, t);
             W += w;
-            O += w * p.part_o[(rec0 + s) * p.head_dim + d];
+            const float *src = p.part_o + (rec0 + s0 + t) * D + lane * kPer;
+            if constexpr (kPer == 4) {
+                const float4 v = *reinterpret_cast<const float4 *>(src);
+                O[0] += w * v.x;
+                O[1] += w * v.y;
+                O[2] += w * v.z;
+                O[3] += w * v.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) O[i] += w * src[i];
+            }
         }
-        T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * p.head_dim + d;
-        *out = Elem<T>::from_float(W > 0.f ? O / W : 0.f);   // partials carry v_scale
-        if (p.lse != nullptr && d == 0)
-            p.lse[(int64_t)h * p.total_q + qrow] =
-                W > 0.f ? (Mu + log2f(W)) * 0.6931471805599453f : -INFINITY;
     }
+    const float inv = W > 0.f ? 1.f / W : 0.f;   // partials carry v_scale
+    T *out = static_cast<T *>(p.out) + ((int64_t)qrow * p.num_heads + h) * D + lane * kPer;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) out[i] = Elem<T>::from_float(O[i] * inv);
+    if (p.lse != nullptr && lane == 0)
+        p.lse[(int64_t)h * p.total_q + qrow] =
+            W > 0.f ? (Mu + log2f(W)) * 0.6931471805599453f : -INFINITY;
 }
 
 // ---- host side ------------------------------------------------------------------
@@ -556,7 +581,8 @@ static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (p.max_splits > 1) {
-        fa_decode_merge_kernel<T><<<p.batch * p.num_heads, 128, 0, stream>>>(p);
+        const int recs = p.batch * p.num_heads;
+        fa_decode_merge_kernel<T, D><<<(recs + 3) / 4, 128, 0, stream>>>(p);
         e = cudaGetLastError();
     }
     return e;

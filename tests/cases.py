@@ -131,6 +131,10 @@ ATTN_CASES = {
                                    "normal", 44),
     "f16_generic_d96": _fa([33, 1], [40, 77], 6, 3, 96, 16, 16, "f16", "normal", 45),
     "bf16_generic_bs4": _fa([9], [23], 4, 2, 128, 4, 16, "bf16", "normal", 46),
+    # pages larger than a 128-token tile (prefill boxes of 128 rows at a row offset) and
+    # head_dim 256 (generic kernel)
+    "bf16_bs256_prefill": _fa([300, 77], [700, 77], 16, 4, 128, 256, 12, "bf16", "normal", 49),
+    "f16_d256_generic": _fa([20, 1], [45, 90], 4, 2, 256, 16, 16, "f16", "normal", 63),
     # empty sequences inside a batch (q_len 0, and q_len = kv_len = 0); the reference
     # golden raises on q_len 0 < kv_len (its mask shape), so these have no fixture
     "edge_empty_seqs_prefill": _fa([0, 100, 0, 37], [10, 300, 0, 37], 32, 8, 128, 16, 64, "bf16",

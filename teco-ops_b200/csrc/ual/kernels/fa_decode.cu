@@ -16,8 +16,11 @@
 //  * warp 4 is a TMA producer: each 16-token page chunk of K and V is one box (per
 //    64 columns) of a 4-D tensor map over the paged cache, with the page id as a
 //    coordinate (out-of-range ids read as zeros) and 128-byte swizzle, into a
-//    8-stage mbarrier ring (3 CTAs per SM, so up to 24 pages of K and V in flight
-//    per SM); block-table ids are fetched 32 chunks at a time;
+//    mbarrier ring (8 stages and 3 CTAs per SM for 16-bit caches, 24 stages and
+//    2 CTAs per SM for e4m3, so 192 KB of K and V in flight per SM); block-table ids
+//    are fetched 32 chunks at a time and the chunks are issued 4 (8 for e4m3) at a
+//    time, one per lane (a single issuing lane measured ~550 cycles per chunk and
+//    left the consumers waiting);
 //  * warps 0-3 consume chunks round-robin: QK^T and PV on the warp MMA
 //    (m16n8k16, fp32 accumulate) fed by conflict-free ldmatrix on the swizzled
 //    tiles, online softmax in the exp2 domain with the O rescale skipped when no
@@ -36,10 +39,15 @@
 //    same slot; one launch replaces the scatter kernel + decode.
 //  * cache layouts [pages, Hkv, bs, D] and [pages, bs, Hkv, D] differ only in the
 //    tensor maps' strides.  An e4m3 cache (FP8) is loaded raw (half the bytes) into
-//    the ring; each consumer warp converts its chunk to f16 (exact for e4m3) into a
-//    private 128B-swizzled staging tile, releases the ring stage at once and runs the
-//    same ldmatrix/MMA code in f16 (Q converted to f16 once).  k_scale is folded into
-//    the softmax scale and v_scale into the output.
+//    the ring, swizzled at its row width; each consumer warp reads its chunk straight
+//    into registers with conflict-free 16-byte loads, releases the ring stage at once
+//    and converts the bytes into f16 MMA fragments (exact for e4m3).  The fragments
+//    need no transposed load because two index orders are free: QK^T sums over the
+//    head dimension, so lane (g, c) takes the D/4 contiguous bytes at (D/4)*c of a key
+//    row (Q is loaded in the same order), and PV's output column n of n-tile nn is
+//    stored as d = (D/8)*n + nn, so the lane takes D/8 contiguous bytes of four value
+//    rows and pairs them with a byte permute.  k_scale is folded into the softmax
+//    scale and v_scale into the output.
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
@@ -58,7 +66,6 @@ namespace kern {
 namespace {
 
 constexpr int kChunk = 16;        // tokens per ring stage (one MMA n-tile pair)
-constexpr int kStages = 8;        // multiple of the 4 consumer warps
 constexpr int kConsumers = 4;
 constexpr int kThreads = 32 * (kConsumers + 1);
 
@@ -69,11 +76,16 @@ struct DecodeSmem {
     static constexpr int kTileBytes = kHalves * kHalfBytes;    // 16-bit K or V of one chunk
     static constexpr int kRawTileBytes = FP8 ? kChunk * D : kTileBytes;   // as loaded
     static constexpr int kStageBytes = 2 * kRawTileBytes;
+    // ring stages, a multiple of the 4 consumer warps.  The page gathers are latency
+    // bound, so the bytes in flight per SM set the bandwidth: 3 CTAs x 8 stages x 8 KB
+    // for 16-bit caches, 2 CTAs x 24 stages x 4 KB for e4m3.
+    static constexpr int kStages = FP8 ? 24 : 8;
+    // chunks the producer issues at once (a power of two dividing 32, below kStages:
+    // a batch never waits for a stage that it fills itself)
+    static constexpr int kBatch = FP8 ? 8 : 4;
     static constexpr int kRingBytes = kStages * kStageBytes;
-    // FP8: per consumer warp a 16-bit K and V staging tile after the ring
-    static constexpr int kStageTiles = FP8 ? kConsumers * 2 * kTileBytes : 0;
     static constexpr int kMergeBytes = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
-    static constexpr int kUsed = kRingBytes + kStageTiles;
+    static constexpr int kUsed = kRingBytes;
     static constexpr int kBytes = (kUsed > kMergeBytes ? kUsed : kMergeBytes) + 1024;
 };
 
@@ -89,6 +101,19 @@ __device__ __forceinline__ void e4m3x16_to_f16(const uint4 &in, uint4 &lo, uint4
     e4m3x4_to_f16(in.y, lo.z, lo.w);
     e4m3x4_to_f16(in.z, hi.x, hi.y);
     e4m3x4_to_f16(in.w, hi.z, hi.w);
+}
+
+// byte offset of 16-byte chunk `ch` of row `r` in an e4m3 [16][D] tile as the TMA
+// swizzle at the row width stores it (D = 128: 128-byte swizzle, D = 64: 64-byte)
+template <int D>
+__device__ __forceinline__ uint32_t swz_fp8(int r, int ch) {
+    if constexpr (D == 128) return (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4));
+    else return (uint32_t)(r * 64 + ((ch ^ ((r >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
 }
 
 // bf16x2 / f16x2 word -> f16x2 word
@@ -110,16 +135,29 @@ __device__ __forceinline__ uint32_t swz128(int r, int ch) {
 
 }  // namespace
 
-// FP8: 2 CTAs per SM (the conversion needs registers; a stage holds half the bytes)
+// FP8: 2 CTAs per SM (the raw key/value words and their conversions need registers)
+#ifdef TECOOPS_DECODE_TRACE
+// Development-only timeline capture (not built into the library): per-chunk clock64()
+// stamps of the consumers and producer of CTAs (0, 0, z < 64).
+__device__ long long g_decode_trace[64 * 4 * 16 * 8];
+__device__ long long g_decode_trace_p[64 * 64];
+extern "C" int tecoops_decode_trace_read_p(long long *host, size_t n) {
+    return (int)cudaMemcpyFromSymbol(host, g_decode_trace_p, n * sizeof(long long));
+}
+extern "C" int tecoops_decode_trace_read(long long *host, size_t n) {
+    return (int)cudaMemcpyFromSymbol(host, g_decode_trace, n * sizeof(long long));
+}
+#endif
 template <typename T, int D, bool FP8>
 __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
     fa_decode_splitkv_kernel(const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, DecodeParams p) {
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
+    using Sm = DecodeSmem<D, FP8>;
+    constexpr int kStages = Sm::kStages;
     __shared__ __align__(8) uint64_t bars[2 * kStages];
     __shared__ int abort_flag;
-    using Sm = DecodeSmem<D, FP8>;
     using MT = typename std::conditional<FP8, __half, T>::type;   // MMA operand type
 
     const int split = blockIdx.x;
@@ -196,7 +234,12 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
             tma_prefetch_desc(&vmap);
         }
         const int *bt = p.block_table + (int64_t)b * p.block_table_dim;
+        // Chunks are issued kBatch at a time, one per lane: lane i waits for its own
+        // stage to be released and issues its chunk's copies, so the per-chunk cost is
+        // one lane's work rather than a serial loop through lane 0.
+        constexpr int kBatch = Sm::kBatch;
         bool ok = true;
+        int issued = 0;   // chunks [0, issued) have their copies in flight or landed
         for (int g0 = 0; ok && g0 < nch; g0 += 32) {
             // page id and in-page row of chunk g0 + lane
             int blk = p.num_pages, row = 0;
@@ -209,21 +252,26 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
                 if (blk < 0 || blk >= p.num_pages) blk = p.num_pages;   // read as zeros
             }
             const int cnt = min(32, nch - g0);
-            for (int i = 0; i < cnt; ++i) {
+            for (int b0 = 0; b0 < cnt; b0 += kBatch) {
+                const int i = b0 + (lane & (kBatch - 1));
+                const int bi = __shfl_sync(0xffffffffu, blk, i & 31);
+                const int ri = __shfl_sync(0xffffffffu, row, i & 31);
                 const int ci = g0 + i;
-                const int bi = __shfl_sync(0xffffffffu, blk, i);
-                const int ri = __shfl_sync(0xffffffffu, row, i);
-                if (lane == 0) {
+                bool lok = true;
+                if (lane < kBatch && i < cnt) {
                     const int st = ci % kStages;
-                    if (ci >= kStages &&
-                        !mbar_wait_bounded(EMPTY(st), ((ci / kStages) - 1) & 1, abortp, p.dev_error,
-                                           0x1100 + (ci & 0xff)))
-                        ok = false;
-                    if (ok) {
+                    if (ci >= kStages)
+                        lok = mbar_wait_bounded(EMPTY(st), ((ci / kStages) - 1) & 1, abortp,
+                                                p.dev_error, 0x1100 + (ci & 0xff));
+#ifdef TECOOPS_DECODE_TRACE
+                    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z < 64 && ci < 64)
+                        g_decode_trace_p[blockIdx.z * 64 + ci] = clock64();
+#endif
+                    if (lok) {
                         mbar_arrive_expect_tx(FULL(st), Sm::kStageBytes);
                         const uint32_t kd = sbase + st * Sm::kStageBytes;
                         const uint32_t vd = kd + Sm::kRawTileBytes;
-                        if (FP8) {   // one unswizzled box of 16 rows x D bytes
+                        if (FP8) {   // one box of 16 rows x D bytes
                             tma_load_4d(kd, &kmap, FULL(st), 0, ri, kvh, bi);
                             tma_load_4d(vd, &vmap, FULL(st), 0, ri, kvh, bi);
                         } else {
@@ -237,13 +285,16 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
                         }
                     }
                 }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
+                ok = __all_sync(0xffffffffu, lok);
                 if (!ok) break;
+                issued = g0 + min(cnt, b0 + kBatch);
             }
         }
-        // on abort: wait (bounded) for this warp's copies still in flight
+        // on abort: wait (bounded) for this warp's copies still in flight (a batch cut
+        // short by the abort may have issued a few more: they are waited for as well)
         if (*abortp && lane == 0) {
-            for (int ci = nch - kStages < 0 ? 0 : nch - kStages; ci < nch; ++ci)
+            const int hi = min(nch, issued + kBatch);
+            for (int ci = hi - kStages < 0 ? 0 : hi - kStages; ci < hi; ++ci)
                 mbar_wait_bounded(FULL(ci % kStages), (ci / kStages) & 1, nullptr, nullptr, 0,
                                   100000000ull);
         }
@@ -255,15 +306,18 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
                 static_cast<const T *>(p.q) + ((int64_t)qrow * p.num_heads + head0) * D;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
-                const int k0 = kk * 16 + 2 * c;
+                // k pairs (2c, 2c+1) and (2c+8, 2c+9) of k-step kk; the FP8 path reads
+                // them at d = (D/4)*c + 4*kk + {0,1} and {2,3} (the key order below)
+                const int k0 = FP8 ? (D / 4) * c + 4 * kk : kk * 16 + 2 * c;
+                const int hi = FP8 ? 1 : 4;   // words from the first pair to the second
                 const uint32_t *r0 =
                     reinterpret_cast<const uint32_t *>(qbase + (int64_t)g * D + k0);
                 const uint32_t *r1 =
                     reinterpret_cast<const uint32_t *>(qbase + (int64_t)(g + 8) * D + k0);
                 qa[kk][0] = g < rows ? __ldg(r0) : 0u;
                 qa[kk][1] = g + 8 < rows ? __ldg(r1) : 0u;
-                qa[kk][2] = g < rows ? __ldg(r0 + 4) : 0u;
-                qa[kk][3] = g + 8 < rows ? __ldg(r1 + 4) : 0u;
+                qa[kk][2] = g < rows ? __ldg(r0 + hi) : 0u;
+                qa[kk][3] = g + 8 < rows ? __ldg(r1 + hi) : 0u;
                 if (FP8) {   // the MMAs run in f16 against the converted cache
 #pragma unroll
                     for (int i = 0; i < 4; ++i) qa[kk][i] = to_f16x2<T>(qa[kk][i]);
@@ -273,83 +327,114 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
         const float sl2 = p.scale_log2;
         const int mi = lane >> 3;   // ldmatrix matrix index of this lane's address
         const int ri = lane & 7;
+#ifdef TECOOPS_DECODE_TRACE
+        const bool trc = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z < 64 && lane == 0;
+        long long *trp = g_decode_trace + ((blockIdx.z * 4 + warp) * 16) * 8;
+        long long tprev = clock64();
+#define DTRACE(i, e) do { if (trc && (i) < 16) trp[(i) * 8 + (e)] = clock64(); } while (0)
+#define DTRACE_DEP(x) do { if (trc && (x) == 12345.f) trp[0] = 0; } while (0)   // orders the stamp
+#else
+#define DTRACE(i, e) do {} while (0)
+#define DTRACE_DEP(x) do {} while (0)
+#endif
         for (int ci = warp; ci < nch; ci += kConsumers) {
             const int st = ci % kStages;
+            DTRACE(ci / 4, 0);
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(FULL(st), (ci / kStages) & 1, abortp,
                                                            p.dev_error, 0x1200 + (ci & 0xff))))
                 break;
+            DTRACE(ci / 4, 1);
             const int tok0 = kv_begin + ci * kChunk;
             const int nv = kv_end - tok0;   // tokens of this chunk before kv_end
             const int nlo = kv_lo - tok0;   // tokens of this chunk before the window
-            uint32_t ktile = sbase + st * Sm::kStageBytes;
-            uint32_t vtile = ktile + Sm::kRawTileBytes;
-            if (FP8) {
-                // convert the raw e4m3 chunk into this warp's 16-bit staging tiles (V rows
-                // past kv_len as zeros: their bytes may be NaN patterns), then free the stage
-                const uint32_t sk = sbase + Sm::kRingBytes + warp * 2 * Sm::kTileBytes;
+            const uint32_t ktile = sbase + st * Sm::kStageBytes;
+            const uint32_t vtile = ktile + Sm::kRawTileBytes;
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            uint32_t vw[4][FP8 ? D / 32 : 1];   // FP8: value rows 2c, 2c+1, 2c+8, 2c+9
+            if constexpr (FP8) {
+                // raw e4m3 chunk -> registers, then the stage is free for the next copy
                 const uint8_t *rk = sgen + (ktile - sbase);
                 const uint8_t *rv = rk + Sm::kRawTileBytes;
-                uint8_t *gk = sgen + (sk - sbase);
-                uint8_t *gv = gk + Sm::kTileBytes;
-                __syncwarp();   // the previous chunk's ldmatrix reads of the staging tiles
+                uint32_t kw[2][D / 16];   // key rows g and g + 8: D/4 bytes at (D/4)*c
 #pragma unroll
-                for (int i = 0; i < (kChunk * D / 16) / 32; ++i) {
-                    const int idx = lane + 32 * i;
-                    const int r = idx / (D / 16);
-                    const int c16 = idx - r * (D / 16);
-                    uint4 lo, hi;
-                    e4m3x16_to_f16(*reinterpret_cast<const uint4 *>(rk + r * D + c16 * 16), lo, hi);
-                    *reinterpret_cast<uint4 *>(gk + swz128(r, 2 * c16)) = lo;
-                    *reinterpret_cast<uint4 *>(gk + swz128(r, 2 * c16 + 1)) = hi;
-                    if (r < nv) {
-                        e4m3x16_to_f16(*reinterpret_cast<const uint4 *>(rv + r * D + c16 * 16),
-                                       lo, hi);
-                    } else {
-                        lo = hi = make_uint4(0, 0, 0, 0);
+                for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                    for (int q = 0; q < D / 64; ++q) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(
+                            rk + swz_fp8<D>(8 * j + g, (D / 64) * c + q));
+                        kw[j][4 * q] = v.x;
+                        kw[j][4 * q + 1] = v.y;
+                        kw[j][4 * q + 2] = v.z;
+                        kw[j][4 * q + 3] = v.w;
                     }
-                    *reinterpret_cast<uint4 *>(gv + swz128(r, 2 * c16)) = lo;
-                    *reinterpret_cast<uint4 *>(gv + swz128(r, 2 * c16 + 1)) = hi;
+                }
+                // value rows past kv_len as zeros (their bytes may be NaN patterns)
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int r = 2 * c + (t & 1) + 8 * (t >> 1);
+                    if constexpr (D == 128) {
+                        uint4 v = *reinterpret_cast<const uint4 *>(rv + swz_fp8<D>(r, g));
+                        if (r >= nv) v = make_uint4(0, 0, 0, 0);
+                        vw[t][0] = v.x;
+                        vw[t][1] = v.y;
+                        vw[t][2] = v.z;
+                        vw[t][3] = v.w;
+                    } else {
+                        uint2 v = *reinterpret_cast<const uint2 *>(rv + swz_fp8<D>(r, g >> 1) +
+                                                                   8 * (g & 1));
+                        if (r >= nv) v = make_uint2(0, 0);
+                        vw[t][0] = v.x;
+                        vw[t][1] = v.y;
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(EMPTY(st));
-                ktile = sk;
-                vtile = sk + Sm::kTileBytes;
-            }
-            if (!FP8 && nv < kChunk) {
-                // V rows past kv_len may hold arbitrary bits (unwritten slots): clear them
-                uint8_t *vt = sgen + (vtile - sbase);
-                for (int idx = lane; idx < (kChunk - nv) * (D / 8); idx += 32) {
-                    const int r = nv + idx / (D / 8);
-                    const int ch = idx % (D / 8);
-                    *reinterpret_cast<uint4 *>(vt + swz128(r, ch)) = make_uint4(0, 0, 0, 0);
-                }
-                fence_proxy_async_smem();   // ordered before TMA refills this stage
-                __syncwarp();
-            }
-            const int rn = kv_len - 1 - tok0;   // row of the new token in this chunk
-            if (fused && rn >= 0 && rn < kChunk) {
-                // the new token's K and V come from the inputs, not from the cache
-                uint8_t *kt = sgen + (ktile - sbase);
-                uint8_t *vt = kt + Sm::kTileBytes;
-                const int64_t src = ((int64_t)qrow * p.num_kv_heads + kvh) * D;
-                for (int ch = lane; ch < D / 8; ch += 32) {
-                    *reinterpret_cast<uint4 *>(kt + swz128(rn, ch)) =
-                        __ldg(reinterpret_cast<const uint4 *>(p.new_key) + (src >> 3) + ch);
-                    *reinterpret_cast<uint4 *>(vt + swz128(rn, ch)) =
-                        __ldg(reinterpret_cast<const uint4 *>(p.new_value) + (src >> 3) + ch);
-                }
-                fence_proxy_async_smem();   // ordered before TMA refills this stage
-                __syncwarp();
-            }
-            // S = Q K^T: two n-tiles of 8 tokens
-            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                // S = Q K^T: the key bytes of k-step kk are word kk of the lane's segment
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-                uint32_t kb[4];
-                const int r = (mi >> 1) * 8 + ri;
-                ldmatrix_x4(kb, ktile + swz128(r, 2 * kk + (mi & 1)));
-                mma16816<MT>(s[0], qa[kk], kb[0], kb[1]);
-                mma16816<MT>(s[1], qa[kk], kb[2], kb[3]);
+                for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        uint32_t b0, b1;
+                        e4m3x4_to_f16(kw[j][kk], b0, b1);
+                        mma16816<__half>(s[j], qa[kk], b0, b1);
+                    }
+                }
+            } else {
+                if (nv < kChunk) {
+                    // V rows past kv_len may hold arbitrary bits (unwritten slots): clear them
+                    uint8_t *vt = sgen + (vtile - sbase);
+                    for (int idx = lane; idx < (kChunk - nv) * (D / 8); idx += 32) {
+                        const int r = nv + idx / (D / 8);
+                        const int ch = idx % (D / 8);
+                        *reinterpret_cast<uint4 *>(vt + swz128(r, ch)) = make_uint4(0, 0, 0, 0);
+                    }
+                    fence_proxy_async_smem();   // ordered before TMA refills this stage
+                    __syncwarp();
+                }
+                const int rn = kv_len - 1 - tok0;   // row of the new token in this chunk
+                if (fused && rn >= 0 && rn < kChunk) {
+                    // the new token's K and V come from the inputs, not from the cache
+                    uint8_t *kt = sgen + (ktile - sbase);
+                    uint8_t *vt = kt + Sm::kTileBytes;
+                    const int64_t src = ((int64_t)qrow * p.num_kv_heads + kvh) * D;
+                    for (int ch = lane; ch < D / 8; ch += 32) {
+                        *reinterpret_cast<uint4 *>(kt + swz128(rn, ch)) =
+                            __ldg(reinterpret_cast<const uint4 *>(p.new_key) + (src >> 3) + ch);
+                        *reinterpret_cast<uint4 *>(vt + swz128(rn, ch)) =
+                            __ldg(reinterpret_cast<const uint4 *>(p.new_value) + (src >> 3) + ch);
+                    }
+                    fence_proxy_async_smem();   // ordered before TMA refills this stage
+                    __syncwarp();
+                }
+                // S = Q K^T: two n-tiles of 8 tokens
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    uint32_t kb[4];
+                    const int r = (mi >> 1) * 8 + ri;
+                    ldmatrix_x4(kb, ktile + swz128(r, 2 * kk + (mi & 1)));
+                    mma16816<MT>(s[0], qa[kk], kb[0], kb[1]);
+                    mma16816<MT>(s[1], qa[kk], kb[2], kb[3]);
+                }
             }
             float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
@@ -364,6 +449,8 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
                     mx[e >> 1] = fmaxf(mx[e >> 1], x);
                 }
             }
+            DTRACE_DEP(mx[0]);
+            DTRACE(ci / 4, 2);
             float mu[2], alpha[2];
             bool grow = false;
 #pragma unroll
@@ -397,23 +484,42 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
                     o[n][3] *= alpha[1];
                 }
             }
+            DTRACE_DEP(alpha[0]);
+            DTRACE(ci / 4, 3);
             uint32_t pa[4];
             pa[0] = Elem<MT>::pack2(s[0][0], s[0][1]);
             pa[1] = Elem<MT>::pack2(s[0][2], s[0][3]);
             pa[2] = Elem<MT>::pack2(s[1][0], s[1][1]);
             pa[3] = Elem<MT>::pack2(s[1][2], s[1][3]);
+            if constexpr (FP8) {
+                // b0 = V[2c][d], V[2c+1][d]; b1 = V[2c+8][d], V[2c+9][d] with
+                // d = (D/8)*g + nn: byte nn of the lane's value segments, paired by row
 #pragma unroll
-            for (int nn = 0; nn < D / 16; ++nn) {
-                uint32_t vb[4];
-                const int r = (mi & 1) * 8 + ri;
-                ldmatrix_x4_trans(vb, vtile + swz128(r, 2 * nn + (mi >> 1)));
-                mma16816<MT>(o[2 * nn], pa, vb[0], vb[1]);
-                mma16816<MT>(o[2 * nn + 1], pa, vb[2], vb[3]);
+                for (int w = 0; w < D / 32; ++w) {
+                    uint32_t b0[4], b1[4];
+                    e4m3x4_to_f16(prmt(vw[0][w], vw[1][w], 0x5140u), b0[0], b0[1]);
+                    e4m3x4_to_f16(prmt(vw[0][w], vw[1][w], 0x7362u), b0[2], b0[3]);
+                    e4m3x4_to_f16(prmt(vw[2][w], vw[3][w], 0x5140u), b1[0], b1[1]);
+                    e4m3x4_to_f16(prmt(vw[2][w], vw[3][w], 0x7362u), b1[2], b1[3]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) mma16816<__half>(o[4 * w + i], pa, b0[i], b1[i]);
+                }
+            } else {
+#pragma unroll
+                for (int nn = 0; nn < D / 16; ++nn) {
+                    uint32_t vb[4];
+                    const int r = (mi & 1) * 8 + ri;
+                    ldmatrix_x4_trans(vb, vtile + swz128(r, 2 * nn + (mi >> 1)));
+                    mma16816<MT>(o[2 * nn], pa, vb[0], vb[1]);
+                    mma16816<MT>(o[2 * nn + 1], pa, vb[2], vb[3]);
+                }
             }
             if (!FP8) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(EMPTY(st));
             }
+            DTRACE_DEP(o[0][0]);
+            DTRACE(ci / 4, 4);
         }
         l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
         l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
@@ -428,11 +534,13 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
     if (warp < kConsumers) {
 #pragma unroll
         for (int n = 0; n < D / 8; ++n) {
-            const int col = n * 8 + 2 * c;
-            so[(warp * 16 + g) * D + col] = o[n][0];
-            so[(warp * 16 + g) * D + col + 1] = o[n][1];
-            so[(warp * 16 + g + 8) * D + col] = o[n][2];
-            so[(warp * 16 + g + 8) * D + col + 1] = o[n][3];
+            // output column of (n-tile n, MMA column 2c / 2c+1); FP8: d = (D/8)*col + n
+            const int col0 = FP8 ? (D / 8) * (2 * c) + n : n * 8 + 2 * c;
+            const int col1 = FP8 ? col0 + D / 8 : col0 + 1;
+            so[(warp * 16 + g) * D + col0] = o[n][0];
+            so[(warp * 16 + g) * D + col1] = o[n][1];
+            so[(warp * 16 + g + 8) * D + col0] = o[n][2];
+            so[(warp * 16 + g + 8) * D + col1] = o[n][3];
         }
         if (c == 0) {
             sml[(warp * 16 + g) * 2 + 0] = m_r[0];

@@ -36,7 +36,8 @@ enum class CacheElem { F16, BF16, E4M3 };
 //   layout 0: [pages, Hkv, block_size, D]   layout 1: [pages, block_size, Hkv, D]
 // (the strides differ, the coordinate order does not, so kernels are layout-blind).
 // Box {box_cols, box_rows, 1, 1}; 16-bit caches use 64-column boxes with 128-byte
-// swizzle, e4m3 caches one unswizzled box of D bytes per row.  Page ids are TMA
+// swizzle, e4m3 caches one box of D bytes per row, swizzled at the row width (128-byte
+// swizzle for D = 128, 64-byte for D = 64, none otherwise).  Page ids are TMA
 // coordinates, so an out-of-range page reads as zeros.
 inline bool encode_cache_map(CUtensorMap *map, const void *base, CacheElem elem, int head_dim,
                              int block_size, int kv_heads, int pages, int box_rows,
@@ -64,7 +65,9 @@ inline bool encode_cache_map(CUtensorMap *map, const void *base, CacheElem elem,
                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     return enc(map, dt, 4, const_cast<void *>(base), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE,
-               fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+               !fp8 || head_dim == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+               : head_dim == 64        ? CU_TENSOR_MAP_SWIZZLE_64B
+                                       : CU_TENSOR_MAP_SWIZZLE_NONE,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

@@ -127,6 +127,9 @@ ATTN_CASES = {
                             "normal", 41),
     "bf16_d64_bs64": _fa([130, 7], [130, 300], 16, 4, 64, 64, 16, "bf16", "normal", 42),
     "f16_bs8_gqa8": _fa([65], [90], 16, 2, 128, 8, 40, "f16", "normal", 43),
+    # decode at head_dim 64 (no reference golden: checked against the oracle only)
+    "bf16_decode_d64_bs32": _fa([1] * 5, [1, 33, 300, 1000, 2047], 16, 4, 64, 32, 200, "bf16",
+                                "normal", 71, golden=False),
     "bf16_decode_gqa16_bs128": _fa([1, 1, 1], [700, 129, 2000], 16, 1, 128, 128, 40, "bf16",
                                    "normal", 44),
     "f16_generic_d96": _fa([33, 1], [40, 77], 6, 3, 96, 16, 16, "f16", "normal", 45),

@@ -95,7 +95,8 @@ def test_reshape_fp8_bit_exact(name, layout, ks, vs):
     assert np.array_equal(dv.cpu().numpy(), ev)
 
 
-def _attn_ex(q, kc, vc, ql, kl, bt, cache_dt, kv_layout=0, k_scale=1.0, v_scale=1.0, max_q=None):
+def _attn_ex(q, kc, vc, ql, kl, bt, cache_dt, kv_layout=0, k_scale=1.0, v_scale=1.0, max_q=None,
+             **opts):
     from gpu_util import handle
     from tecoops import capi
     dt = capi.DATA_HALF if q.dtype == torch.float16 else capi.DATA_BFLOAT16
@@ -106,7 +107,7 @@ def _attn_ex(q, kc, vc, ql, kl, bt, cache_dt, kv_layout=0, k_scale=1.0, v_scale=
     st = capi.flash_attention_ex(handle(), mq, int(kl.max().item()), kc.shape[0], ql.data_ptr(),
                                  kl.data_ptr(), d_bt, bt.data_ptr(), d_q, q.data_ptr(), d_c,
                                  kc.data_ptr(), d_c, vc.data_ptr(), d_q, out.data_ptr(), 0,
-                                 kv_layout=kv_layout, k_scale=k_scale, v_scale=v_scale)
+                                 kv_layout=kv_layout, k_scale=k_scale, v_scale=v_scale, **opts)
     capi.check(st, "tecoopsFlashAttentionEx")
     torch.cuda.synchronize()
     return out
@@ -129,7 +130,10 @@ def test_attention_vllm_layout_matches_reference_layout(name):
 
 @pytest.mark.parametrize("name,layout", [("bf16_bs16_decode", 0), ("api_decode_2x128", 1),
                                          ("bf16_decode_gqa16_bs128", 0), ("f16_generic_d96", 0),
-                                         ("bf16_bs16_varlen", 1), ("bf16_d64_bs64", 0)])
+                                         ("bf16_bs16_varlen", 1), ("bf16_d64_bs64", 0),
+                                         ("bf16_decode_d64_bs32", 0), ("bf16_decode_d64_bs32", 1),
+                                         ("opt_window_decode_bf16", 1),
+                                         ("opt_window700_decode_f16", 0)])
 def test_attention_fp8_cache_vs_oracle(name, layout):
     """e4m3 caches: decode on the split-KV kernel (f16 MMAs on converted tiles),
     prefill on the tcgen05 kernel over a dequantised compact copy, odd shapes on the
@@ -147,13 +151,16 @@ def test_attention_fp8_cache_vs_oracle(name, layout):
     else:
         kd, vd = torch.from_numpy(kq).cuda(), torch.from_numpy(vq).cuda()
     q = words_to_dev(inp["q"], c["dtype"])
+    oo = cases.attn_opts(c)
     out = _attn_ex(q, kd, vd, torch.from_numpy(inp["q_lens"]).cuda(),
                    torch.from_numpy(inp["kv_lens"]).cuda(),
                    torch.from_numpy(inp["block_table"]).cuda(), capi.DATA_FLOAT8_E4M3,
-                   kv_layout=layout, k_scale=ks, v_scale=vs)
+                   kv_layout=layout, k_scale=ks, v_scale=vs,
+                   softmax_scale=oo["softmax_scale"] or 0.0, causal=oo["causal"],
+                   window=oo["window"])
     ref = oracle.flash_attn_varlen(seeded.words_to_f32(inp["q"], c["dtype"]),
                                    fp8.dequantize(kq, ks), fp8.dequantize(vq, vs),
-                                   inp["q_lens"], inp["kv_lens"], inp["block_table"])
+                                   inp["q_lens"], inp["kv_lens"], inp["block_table"], **oo)
     o = out.float().cpu().numpy()
     assert np.isfinite(o).all()
     mx, mean, diff1 = errors(o, ref)
@@ -226,3 +233,30 @@ def test_fp8_prefill_config2_full_size():
                                    fp8.dequantize(vc.cpu().numpy(), vs), lens, lens, bt.numpy())
     mx, mean, diff1 = errors(out.float().cpu().numpy(), ref)
     assert mx <= 2e-2 and mean <= 2e-3 and diff1 <= 1e-2, (mx, mean, diff1)
+
+
+def test_fp8_decode_lse_vs_oracle():
+    """The split-KV decode on an e4m3 cache writes the natural-log log-sum-exp of
+    every row (split partials merged) next to the output."""
+    from gpu_util import errors, words_to_dev
+    from tecoops import capi
+    c = cases.ATTN_CASES["opt_lse_decode_bf16"]
+    inp = cases.attn_inputs(c)
+    ks, vs = 1.0 / 64, 1.0 / 32
+    kq = fp8.quantize(seeded.words_to_f32(inp["k_cache"], c["dtype"]), ks)
+    vq = fp8.quantize(seeded.words_to_f32(inp["v_cache"], c["dtype"]), vs)
+    q = words_to_dev(inp["q"], c["dtype"])
+    lse = torch.full((c["Hq"], q.shape[0]), float("nan"), device="cuda")
+    out = _attn_ex(q, torch.from_numpy(kq).cuda(), torch.from_numpy(vq).cuda(),
+                   torch.from_numpy(inp["q_lens"]).cuda(), torch.from_numpy(inp["kv_lens"]).cuda(),
+                   torch.from_numpy(inp["block_table"]).cuda(), capi.DATA_FLOAT8_E4M3,
+                   k_scale=ks, v_scale=vs, softmax_lse=lse.data_ptr(),
+                   softmax_scale=cases.attn_opts(c)["softmax_scale"] or 0.0)
+    ref, ref_lse = oracle.flash_attn_varlen(seeded.words_to_f32(inp["q"], c["dtype"]),
+                                            fp8.dequantize(kq, ks), fp8.dequantize(vq, vs),
+                                            inp["q_lens"], inp["kv_lens"], inp["block_table"],
+                                            softmax_scale=cases.attn_opts(c)["softmax_scale"],
+                                            return_lse=True)
+    mx, mean, _ = errors(out.float().cpu().numpy(), ref)
+    assert mx <= 2e-2 and mean <= 2e-3, (mx, mean)
+    assert np.allclose(lse.cpu().numpy(), ref_lse, atol=1e-3, rtol=1e-4)

@@ -91,8 +91,9 @@ struct DecodeParams {
 };
 
 bool decode_supported(int head_dim, int block_size, int group);
+// cache_fp8: an e4m3 cache (its CTAs move half the bytes per token, so splits are longer)
 void decode_plan(int num_sms, int batch, int kv_heads, int group, int max_k, int *split_tokens,
-                 int *max_splits);
+                 int *max_splits, bool cache_fp8 = false);
 size_t decode_workspace_bytes(int batch, int num_heads, int head_dim, int max_splits);
 cudaError_t launch_decode(const DecodeParams &p, bool bf16, cudaStream_t stream);
 

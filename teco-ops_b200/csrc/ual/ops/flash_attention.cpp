@@ -47,7 +47,8 @@ static kern::AttnShape toShape(const FlashAttentionArgs &a) {
 
 static void decodePlan(const FlashAttentionArgs &a, int *split, int *max_splits) {
     kern::decode_plan(a.num_sms, a.batch_size, a.local_kv_head_num,
-                      a.local_head_num / a.local_kv_head_num, a.max_k_seq_len, split, max_splits);
+                      a.local_head_num / a.local_kv_head_num, a.max_k_seq_len, split, max_splits,
+                      a.cache_fp8 != 0);
 }
 
 static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {

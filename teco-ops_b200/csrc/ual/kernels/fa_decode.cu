@@ -48,6 +48,11 @@
 //    stored as d = (D/8)*n + nn, so the lane takes D/8 contiguous bytes of four value
 //    rows and pairs them with a byte permute.  k_scale is folded into the softmax
 //    scale and v_scale into the output.
+//  * e4m3 with a GQA group of at most 8 heads runs transposed: S^T = K Q^T puts the 16
+//    tokens of a chunk in the MMA rows and the (<= 8) heads in its 8 columns, and
+//    O^T += V^T P^T (output row d = (D/16)*m + n-tile), so no MMA row is padding: half
+//    the MMAs and exp2 of the head-rows form, 32 accumulator registers instead of 64
+//    and 3 CTAs per SM; P^T reaches the B-operand layout with 4 shuffles per chunk.
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
@@ -69,7 +74,7 @@ constexpr int kChunk = 16;        // tokens per ring stage (one MMA n-tile pair)
 constexpr int kConsumers = 4;
 constexpr int kThreads = 32 * (kConsumers + 1);
 
-template <int D, bool FP8>
+template <int D, bool FP8, bool TP = false>
 struct DecodeSmem {
     static constexpr int kHalves = D / 64;
     static constexpr int kHalfBytes = kChunk * 128;            // 16 rows x 64 columns
@@ -78,8 +83,9 @@ struct DecodeSmem {
     static constexpr int kStageBytes = 2 * kRawTileBytes;
     // ring stages, a multiple of the 4 consumer warps.  The page gathers are latency
     // bound, so the bytes in flight per SM set the bandwidth: 3 CTAs x 8 stages x 8 KB
-    // for 16-bit caches, 2 CTAs x 24 stages x 4 KB for e4m3.
-    static constexpr int kStages = FP8 ? 24 : 8;
+    // for 16-bit caches, 2 CTAs x 24 stages x 4 KB for e4m3 (3 x 16 in the transposed
+    // form, whose smaller register footprint fits 3 CTAs per SM).
+    static constexpr int kStages = FP8 ? (TP ? 16 : 24) : 8;
     // chunks the producer issues at once (a power of two dividing 32, below kStages:
     // a batch never waits for a stage that it fills itself)
     static constexpr int kBatch = FP8 ? 8 : 4;
@@ -148,13 +154,14 @@ extern "C" int tecoops_decode_trace_read(long long *host, size_t n) {
     return (int)cudaMemcpyFromSymbol(host, g_decode_trace, n * sizeof(long long));
 }
 #endif
-template <typename T, int D, bool FP8>
-__global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
+// TP: the transposed form (e4m3 caches with a GQA group of at most 8 heads)
+template <typename T, int D, bool FP8, bool TP>
+__global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
     fa_decode_splitkv_kernel(const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, DecodeParams p) {
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
-    using Sm = DecodeSmem<D, FP8>;
+    using Sm = DecodeSmem<D, FP8, TP>;
     constexpr int kStages = Sm::kStages;
     __shared__ __align__(8) uint64_t bars[2 * kStages];
     __shared__ int abort_flag;
@@ -349,6 +356,128 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
             const int nlo = kv_lo - tok0;   // tokens of this chunk before the window
             const uint32_t ktile = sbase + st * Sm::kStageBytes;
             const uint32_t vtile = ktile + Sm::kRawTileBytes;
+            if constexpr (TP) {
+                // ---- transposed form (e4m3, GQA group <= 8): S^T = K Q^T with the 16
+                // tokens of the chunk as MMA rows and the heads as its 8 columns, then
+                // O^T += V^T P^T, so no MMA row is padding
+                const uint8_t *rk = sgen + (ktile - sbase);
+                const uint8_t *rv = rk + Sm::kRawTileBytes;
+                uint32_t kw[2][D / 16];   // key rows g and g + 8: D/4 bytes at (D/4)*c
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                    for (int q = 0; q < D / 64; ++q) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(
+                            rk + swz_fp8<D>(8 * j + g, (D / 64) * c + q));
+                        kw[j][4 * q] = v.x;
+                        kw[j][4 * q + 1] = v.y;
+                        kw[j][4 * q + 2] = v.z;
+                        kw[j][4 * q + 3] = v.w;
+                    }
+                }
+                // value rows 2c, 2c+1, 2c+8, 2c+9 at output rows m = g and g + 8 of every
+                // m-tile: D/16 bytes at column (D/16)*m (zeros past kv_len)
+                uint32_t tv[4][2][D / 64];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int r = 2 * c + (t & 1) + 8 * (t >> 1);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int m = g + 8 * h;
+                        if constexpr (D == 128) {
+                            uint2 v = *reinterpret_cast<const uint2 *>(
+                                rv + swz_fp8<D>(r, m >> 1) + 8 * (m & 1));
+                            if (r >= nv) v = make_uint2(0, 0);
+                            tv[t][h][0] = v.x;
+                            tv[t][h][1] = v.y;
+                        } else {
+                            uint32_t v = *reinterpret_cast<const uint32_t *>(
+                                rv + swz_fp8<D>(r, m >> 2) + 4 * (m & 3));
+                            tv[t][h][0] = r >= nv ? 0u : v;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(EMPTY(st));
+                // S^T: A = key rows (k-step kk is word kk of the lane's segment), B = Q^T
+                float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    uint32_t af[4];
+                    e4m3x4_to_f16(kw[0][kk], af[0], af[2]);
+                    e4m3x4_to_f16(kw[1][kk], af[1], af[3]);
+                    mma16816<__half>((kk & 1) ? sb : sa, af, qa[kk][0], qa[kk][2]);
+                }
+                // sa[0..1]: token g, heads 2c, 2c+1; sa[2..3]: token g + 8
+                float x[4], mx[2];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int t = g + 8 * (e >> 1);
+                    x[e] = (unsigned)(t - nlo) < (unsigned)(nv - nlo) ? (sa[e] + sb[e]) * sl2
+                                                                      : -INFINITY;
+                }
+                mx[0] = fmaxf(x[0], x[2]);
+                mx[1] = fmaxf(x[1], x[3]);
+                float mu[2], alpha[2];
+                bool grow = false;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                    for (int o2 = 4; o2 < 32; o2 <<= 1)
+                        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], o2));
+                    const float m_new = fmaxf(m_r[h], mx[h]);
+                    grow |= m_new > m_r[h];
+                    mu[h] = m_new == -INFINITY ? 0.f : m_new;
+                    alpha[h] = fast_exp2(m_r[h] - mu[h]);
+                    m_r[h] = m_new;
+                }
+                float pe[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) pe[e] = fast_exp2(x[e] - mu[e & 1]);
+                // per-lane partial row sums (reduced over the 8 token lanes at the end)
+                l_r[0] = l_r[0] * alpha[0] + (pe[0] + pe[2]);
+                l_r[1] = l_r[1] * alpha[1] + (pe[1] + pe[3]);
+                if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+                    for (int n = 0; n < D / 16; ++n) {
+                        o[n][0] *= alpha[0];
+                        o[n][1] *= alpha[1];
+                        o[n][2] *= alpha[0];
+                        o[n][3] *= alpha[1];
+                    }
+                }
+                // P^T as the B operand: b0 = P[2c][head g], P[2c+1][g]; b1 = P[2c+8][g],
+                // P[2c+9][g].  P[t][h] sits in lane 4*(t&7) + h/2, word t/8, half h&1.
+                const uint32_t w0 = Elem<__half>::pack2(pe[0], pe[1]);
+                const uint32_t w1 = Elem<__half>::pack2(pe[2], pe[3]);
+                const int src0 = 4 * (2 * c) + (g >> 1), src1 = src0 + 4;
+                const uint32_t x0 = __shfl_sync(0xffffffffu, w0, src0);
+                const uint32_t x1 = __shfl_sync(0xffffffffu, w0, src1);
+                const uint32_t y0 = __shfl_sync(0xffffffffu, w1, src0);
+                const uint32_t y1 = __shfl_sync(0xffffffffu, w1, src1);
+                const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
+                const uint32_t b0 = prmt(x0, x1, sel), b1 = prmt(y0, y1, sel);
+                // O^T m-tile mt: rows d = (D/16)*m + mt (m = g, g + 8), byte mt of the
+                // lane's value segments, paired by token row
+#pragma unroll
+                for (int w = 0; w < D / 64; ++w) {
+                    uint32_t a0[4], a1[4], a2[4], a3[4];
+                    e4m3x4_to_f16(prmt(tv[0][0][w], tv[1][0][w], 0x5140u), a0[0], a0[1]);
+                    e4m3x4_to_f16(prmt(tv[0][0][w], tv[1][0][w], 0x7362u), a0[2], a0[3]);
+                    e4m3x4_to_f16(prmt(tv[0][1][w], tv[1][1][w], 0x5140u), a1[0], a1[1]);
+                    e4m3x4_to_f16(prmt(tv[0][1][w], tv[1][1][w], 0x7362u), a1[2], a1[3]);
+                    e4m3x4_to_f16(prmt(tv[2][0][w], tv[3][0][w], 0x5140u), a2[0], a2[1]);
+                    e4m3x4_to_f16(prmt(tv[2][0][w], tv[3][0][w], 0x7362u), a2[2], a2[3]);
+                    e4m3x4_to_f16(prmt(tv[2][1][w], tv[3][1][w], 0x5140u), a3[0], a3[1]);
+                    e4m3x4_to_f16(prmt(tv[2][1][w], tv[3][1][w], 0x7362u), a3[2], a3[3]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t af[4] = {a0[i], a1[i], a2[i], a3[i]};
+                        mma16816<__half>(o[4 * w + i], af, b0, b1);
+                    }
+                }
+                continue;
+            }
             float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
             uint32_t vw[4][FP8 ? D / 32 : 1];   // FP8: value rows 2c, 2c+1, 2c+8, 2c+9
             if constexpr (FP8) {
@@ -521,17 +650,42 @@ __global__ void __launch_bounds__(kThreads, FP8 ? 2 : 3)
             DTRACE_DEP(o[0][0]);
             DTRACE(ci / 4, 4);
         }
-        l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
-        l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
-        l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
-        l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
+        if constexpr (TP) {   // partial sums of heads 2c, 2c+1 over the 8 token lanes
+#pragma unroll
+            for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], o2);
+                l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], o2);
+            }
+        } else {
+            l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 1);
+            l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], 2);
+            l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 1);
+            l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], 2);
+        }
     }
 
     // ---- merge the 4 consumer warps through shared memory (the ring is idle now) ----
     __syncthreads();
     float *so = reinterpret_cast<float *>(sgen);   // [4][16][D]
     float *sml = so + 4 * 16 * D;                  // [4][16][2]
-    if (warp < kConsumers) {
+    if (TP && warp < kConsumers) {
+        // O^T m-tile n: rows d = (D/16)*m + n for m = g (o[n][0..1]) and g + 8
+        // (o[n][2..3]), columns = heads 2c, 2c+1
+#pragma unroll
+        for (int n = 0; n < D / 16; ++n) {
+            const int d0 = (D / 16) * g + n, d1 = d0 + D / 2;
+            so[(warp * 16 + 2 * c) * D + d0] = o[n][0];
+            so[(warp * 16 + 2 * c + 1) * D + d0] = o[n][1];
+            so[(warp * 16 + 2 * c) * D + d1] = o[n][2];
+            so[(warp * 16 + 2 * c + 1) * D + d1] = o[n][3];
+        }
+        if (g == 0) {
+            sml[(warp * 16 + 2 * c) * 2 + 0] = m_r[0];
+            sml[(warp * 16 + 2 * c) * 2 + 1] = l_r[0];
+            sml[(warp * 16 + 2 * c + 1) * 2 + 0] = m_r[1];
+            sml[(warp * 16 + 2 * c + 1) * 2 + 1] = l_r[1];
+        }
+    } else if (warp < kConsumers) {
 #pragma unroll
         for (int n = 0; n < D / 8; ++n) {
             // output column of (n-tile n, MMA column 2c / 2c+1); FP8: d = (D/8)*col + n
@@ -672,7 +826,7 @@ size_t decode_workspace_bytes(int batch, int num_heads, int head_dim, int max_sp
     return recs * head_dim * sizeof(float) + recs * sizeof(float) + 256;
 }
 
-template <typename T, int D, bool FP8>
+template <typename T, int D, bool FP8, bool TP>
 static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
     const CacheElem ce = FP8 ? CacheElem::E4M3
                              : std::is_same<T, __half>::value ? CacheElem::F16 : CacheElem::BF16;
@@ -682,8 +836,8 @@ static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
         !encode_cache_map(&vmap, p.value_cache, ce, D, p.block_size, p.num_kv_heads,
                           p.num_pages, kChunk, p.kv_layout))
         return cudaErrorInvalidValue;
-    const int smem = DecodeSmem<D, FP8>::kBytes;
-    auto kfn = fa_decode_splitkv_kernel<T, D, FP8>;
+    const int smem = DecodeSmem<D, FP8, TP>::kBytes;
+    auto kfn = fa_decode_splitkv_kernel<T, D, FP8, TP>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p.max_splits, p.num_kv_heads * p.num_slices, p.batch);
@@ -698,23 +852,25 @@ static cudaError_t launch_decode_t(const DecodeParams &p, cudaStream_t stream) {
     return e;
 }
 
-template <bool FP8>
+template <bool FP8, bool TP>
 static cudaError_t launch_decode_f(const DecodeParams &p, bool bf16, cudaStream_t stream) {
     if (p.head_dim == 128) {
-        return bf16 ? launch_decode_t<__nv_bfloat16, 128, FP8>(p, stream)
-                    : launch_decode_t<__half, 128, FP8>(p, stream);
+        return bf16 ? launch_decode_t<__nv_bfloat16, 128, FP8, TP>(p, stream)
+                    : launch_decode_t<__half, 128, FP8, TP>(p, stream);
     }
     if (p.head_dim == 64) {
-        return bf16 ? launch_decode_t<__nv_bfloat16, 64, FP8>(p, stream)
-                    : launch_decode_t<__half, 64, FP8>(p, stream);
+        return bf16 ? launch_decode_t<__nv_bfloat16, 64, FP8, TP>(p, stream)
+                    : launch_decode_t<__half, 64, FP8, TP>(p, stream);
     }
     return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_decode(const DecodeParams &p, bool bf16, cudaStream_t stream) {
     if (p.cache_fp8 && p.new_key != nullptr) return cudaErrorInvalidValue;
-    return p.cache_fp8 ? launch_decode_f<true>(p, bf16, stream)
-                       : launch_decode_f<false>(p, bf16, stream);
+    if (!p.cache_fp8) return launch_decode_f<false, false>(p, bf16, stream);
+    // e4m3 with a GQA group of at most 8 heads: the transposed (tokens x heads) form
+    if (p.group <= 8) return launch_decode_f<true, true>(p, bf16, stream);
+    return launch_decode_f<true, false>(p, bf16, stream);
 }
 
 }  // namespace kern

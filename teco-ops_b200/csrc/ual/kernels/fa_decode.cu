@@ -48,11 +48,12 @@
 //    stored as d = (D/8)*n + nn, so the lane takes D/8 contiguous bytes of four value
 //    rows and pairs them with a byte permute.  k_scale is folded into the softmax
 //    scale and v_scale into the output.
-//  * e4m3 with a GQA group of at most 8 heads runs transposed: S^T = K Q^T puts the 16
-//    tokens of a chunk in the MMA rows and the (<= 8) heads in its 8 columns, and
-//    O^T += V^T P^T (output row d = (D/16)*m + n-tile), so no MMA row is padding: half
-//    the MMAs and exp2 of the head-rows form, 32 accumulator registers instead of 64
-//    and 3 CTAs per SM; P^T reaches the B-operand layout with 4 shuffles per chunk.
+//  * a GQA group of at most 8 heads runs transposed: S^T = K Q^T puts the 16 tokens of
+//    a chunk in the MMA rows and the (<= 8) heads in its 8 columns, and O^T += V^T P^T
+//    (16-bit: K by ldmatrix, V^T by transposing ldmatrix; e4m3: output row
+//    d = (D/16)*m + n-tile from byte-paired registers), so no MMA row is padding: half
+//    the MMAs and exp2 of the head-rows form and 32 accumulator registers instead of 64
+//    (3 CTAs per SM for e4m3 too); P^T reaches the B-operand layout with 4 shuffles.
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
@@ -154,7 +155,7 @@ extern "C" int tecoops_decode_trace_read(long long *host, size_t n) {
     return (int)cudaMemcpyFromSymbol(host, g_decode_trace, n * sizeof(long long));
 }
 #endif
-// TP: the transposed form (e4m3 caches with a GQA group of at most 8 heads)
+// TP: the transposed form (GQA group of at most 8 heads)
 template <typename T, int D, bool FP8, bool TP>
 __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
     fa_decode_splitkv_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -356,10 +357,43 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
             const int nlo = kv_lo - tok0;   // tokens of this chunk before the window
             const uint32_t ktile = sbase + st * Sm::kStageBytes;
             const uint32_t vtile = ktile + Sm::kRawTileBytes;
+            // 16-bit tiles: V rows past kv_len may hold arbitrary bits (unwritten slots),
+            // so they are cleared; the fused step's new token comes from the inputs
+            auto prep16 = [&]() {
+            if (nv < kChunk) {
+                // V rows past kv_len may hold arbitrary bits (unwritten slots): clear them
+                uint8_t *vt = sgen + (vtile - sbase);
+                for (int idx = lane; idx < (kChunk - nv) * (D / 8); idx += 32) {
+                    const int r = nv + idx / (D / 8);
+                    const int ch = idx % (D / 8);
+                    *reinterpret_cast<uint4 *>(vt + swz128(r, ch)) = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async_smem();   // ordered before TMA refills this stage
+                __syncwarp();
+            }
+            const int rn = kv_len - 1 - tok0;   // row of the new token in this chunk
+            if (fused && rn >= 0 && rn < kChunk) {
+                // the new token's K and V come from the inputs, not from the cache
+                uint8_t *kt = sgen + (ktile - sbase);
+                uint8_t *vt = kt + Sm::kTileBytes;
+                const int64_t src = ((int64_t)qrow * p.num_kv_heads + kvh) * D;
+                for (int ch = lane; ch < D / 8; ch += 32) {
+                    *reinterpret_cast<uint4 *>(kt + swz128(rn, ch)) =
+                        __ldg(reinterpret_cast<const uint4 *>(p.new_key) + (src >> 3) + ch);
+                    *reinterpret_cast<uint4 *>(vt + swz128(rn, ch)) =
+                        __ldg(reinterpret_cast<const uint4 *>(p.new_value) + (src >> 3) + ch);
+                }
+                fence_proxy_async_smem();   // ordered before TMA refills this stage
+                __syncwarp();
+            }
+            };
             if constexpr (TP) {
                 // ---- transposed form (e4m3, GQA group <= 8): S^T = K Q^T with the 16
                 // tokens of the chunk as MMA rows and the heads as its 8 columns, then
                 // O^T += V^T P^T, so no MMA row is padding
+                float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t tv[4][2][FP8 ? D / 64 : 1];
+                if constexpr (FP8) {
                 const uint8_t *rk = sgen + (ktile - sbase);
                 const uint8_t *rv = rk + Sm::kRawTileBytes;
                 uint32_t kw[2][D / 16];   // key rows g and g + 8: D/4 bytes at (D/4)*c
@@ -377,7 +411,6 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                 }
                 // value rows 2c, 2c+1, 2c+8, 2c+9 at output rows m = g and g + 8 of every
                 // m-tile: D/16 bytes at column (D/16)*m (zeros past kv_len)
-                uint32_t tv[4][2][D / 64];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     const int r = 2 * c + (t & 1) + 8 * (t >> 1);
@@ -400,13 +433,23 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(EMPTY(st));
                 // S^T: A = key rows (k-step kk is word kk of the lane's segment), B = Q^T
-                float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     uint32_t af[4];
                     e4m3x4_to_f16(kw[0][kk], af[0], af[2]);
                     e4m3x4_to_f16(kw[1][kk], af[1], af[3]);
                     mma16816<__half>((kk & 1) ? sb : sa, af, qa[kk][0], qa[kk][2]);
+                }
+                } else {
+                    prep16();
+                    // S^T: A = key rows by ldmatrix (matrices: tokens 0-7 / 8-15 x the two
+                    // 8-column halves of k-step kk), B = Q^T
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        uint32_t af[4];
+                        ldmatrix_x4(af, ktile + swz128((mi & 1) * 8 + ri, 2 * kk + (mi >> 1)));
+                        mma16816<MT>((kk & 1) ? sb : sa, af, qa[kk][0], qa[kk][2]);
+                    }
                 }
                 // sa[0..1]: token g, heads 2c, 2c+1; sa[2..3]: token g + 8
                 float x[4], mx[2];
@@ -448,8 +491,8 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                 }
                 // P^T as the B operand: b0 = P[2c][head g], P[2c+1][g]; b1 = P[2c+8][g],
                 // P[2c+9][g].  P[t][h] sits in lane 4*(t&7) + h/2, word t/8, half h&1.
-                const uint32_t w0 = Elem<__half>::pack2(pe[0], pe[1]);
-                const uint32_t w1 = Elem<__half>::pack2(pe[2], pe[3]);
+                const uint32_t w0 = Elem<MT>::pack2(pe[0], pe[1]);
+                const uint32_t w1 = Elem<MT>::pack2(pe[2], pe[3]);
                 const int src0 = 4 * (2 * c) + (g >> 1), src1 = src0 + 4;
                 const uint32_t x0 = __shfl_sync(0xffffffffu, w0, src0);
                 const uint32_t x1 = __shfl_sync(0xffffffffu, w0, src1);
@@ -457,6 +500,7 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                 const uint32_t y1 = __shfl_sync(0xffffffffu, w1, src1);
                 const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
                 const uint32_t b0 = prmt(x0, x1, sel), b1 = prmt(y0, y1, sel);
+                if constexpr (FP8) {
                 // O^T m-tile mt: rows d = (D/16)*m + mt (m = g, g + 8), byte mt of the
                 // lane's value segments, paired by token row
 #pragma unroll
@@ -475,6 +519,18 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                         const uint32_t af[4] = {a0[i], a1[i], a2[i], a3[i]};
                         mma16816<__half>(o[4 * w + i], af, b0, b1);
                     }
+                }
+                } else {
+                    // O^T m-tile mt: rows d = 16*mt + m; A = V^T by transposing loads of the
+                    // value tile (matrices: d 0-7 / 8-15 x tokens 0-7 / 8-15)
+#pragma unroll
+                    for (int mt = 0; mt < D / 16; ++mt) {
+                        uint32_t af[4];
+                        ldmatrix_x4_trans(af, vtile + swz128(8 * (mi >> 1) + ri, 2 * mt + (mi & 1)));
+                        mma16816<MT>(o[mt], af, b0, b1);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(EMPTY(st));
                 }
                 continue;
             }
@@ -529,32 +585,7 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                     }
                 }
             } else {
-                if (nv < kChunk) {
-                    // V rows past kv_len may hold arbitrary bits (unwritten slots): clear them
-                    uint8_t *vt = sgen + (vtile - sbase);
-                    for (int idx = lane; idx < (kChunk - nv) * (D / 8); idx += 32) {
-                        const int r = nv + idx / (D / 8);
-                        const int ch = idx % (D / 8);
-                        *reinterpret_cast<uint4 *>(vt + swz128(r, ch)) = make_uint4(0, 0, 0, 0);
-                    }
-                    fence_proxy_async_smem();   // ordered before TMA refills this stage
-                    __syncwarp();
-                }
-                const int rn = kv_len - 1 - tok0;   // row of the new token in this chunk
-                if (fused && rn >= 0 && rn < kChunk) {
-                    // the new token's K and V come from the inputs, not from the cache
-                    uint8_t *kt = sgen + (ktile - sbase);
-                    uint8_t *vt = kt + Sm::kTileBytes;
-                    const int64_t src = ((int64_t)qrow * p.num_kv_heads + kvh) * D;
-                    for (int ch = lane; ch < D / 8; ch += 32) {
-                        *reinterpret_cast<uint4 *>(kt + swz128(rn, ch)) =
-                            __ldg(reinterpret_cast<const uint4 *>(p.new_key) + (src >> 3) + ch);
-                        *reinterpret_cast<uint4 *>(vt + swz128(rn, ch)) =
-                            __ldg(reinterpret_cast<const uint4 *>(p.new_value) + (src >> 3) + ch);
-                    }
-                    fence_proxy_async_smem();   // ordered before TMA refills this stage
-                    __syncwarp();
-                }
+                prep16();
                 // S = Q K^T: two n-tiles of 8 tokens
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
@@ -669,11 +700,13 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
     float *so = reinterpret_cast<float *>(sgen);   // [4][16][D]
     float *sml = so + 4 * 16 * D;                  // [4][16][2]
     if (TP && warp < kConsumers) {
-        // O^T m-tile n: rows d = (D/16)*m + n for m = g (o[n][0..1]) and g + 8
-        // (o[n][2..3]), columns = heads 2c, 2c+1
+        // O^T m-tile n: output rows m = g (o[n][0..1]) and g + 8 (o[n][2..3]),
+        // columns = heads 2c, 2c+1
 #pragma unroll
         for (int n = 0; n < D / 16; ++n) {
-            const int d0 = (D / 16) * g + n, d1 = d0 + D / 2;
+            // e4m3: d = (D/16)*m + n; 16-bit: d = 16*n + m
+            const int d0 = FP8 ? (D / 16) * g + n : 16 * n + g;
+            const int d1 = FP8 ? d0 + D / 2 : d0 + 8;
             so[(warp * 16 + 2 * c) * D + d0] = o[n][0];
             so[(warp * 16 + 2 * c + 1) * D + d0] = o[n][1];
             so[(warp * 16 + 2 * c) * D + d1] = o[n][2];
@@ -867,10 +900,12 @@ static cudaError_t launch_decode_f(const DecodeParams &p, bool bf16, cudaStream_
 
 cudaError_t launch_decode(const DecodeParams &p, bool bf16, cudaStream_t stream) {
     if (p.cache_fp8 && p.new_key != nullptr) return cudaErrorInvalidValue;
-    if (!p.cache_fp8) return launch_decode_f<false, false>(p, bf16, stream);
-    // e4m3 with a GQA group of at most 8 heads: the transposed (tokens x heads) form
-    if (p.group <= 8) return launch_decode_f<true, true>(p, bf16, stream);
-    return launch_decode_f<true, false>(p, bf16, stream);
+    // a GQA group of at most 8 heads: the transposed (tokens x heads) form
+    if (p.group <= 8)
+        return p.cache_fp8 ? launch_decode_f<true, true>(p, bf16, stream)
+                           : launch_decode_f<false, true>(p, bf16, stream);
+    return p.cache_fp8 ? launch_decode_f<true, false>(p, bf16, stream)
+                       : launch_decode_f<false, false>(p, bf16, stream);
 }
 
 }  // namespace kern

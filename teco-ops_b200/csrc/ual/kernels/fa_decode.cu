@@ -844,8 +844,9 @@ void decode_plan(int num_sms, int batch, int kv_heads, int group, int max_k, int
     const int64_t target = (int64_t)num_sms * 2 * 64;
     int64_t split = (work + target - 1) / target;
     split = ((split + 63) / 64) * 64;
-    // (an e4m3 cache: 3072 tokens per split measured 4 % faster on the B=64 workload)
-    const int64_t smin = cache_fp8 ? 3072 : 1536;
+    // (an e4m3 cache in the head-rows form, GQA group > 8: 3072 tokens per split measured
+    // 4 % faster on the B=64 workload; the transposed form is best at 1536 like 16-bit)
+    const int64_t smin = cache_fp8 && group > 8 ? 3072 : 1536;
     if (split < smin) split = smin;
     const int64_t cap = ((int64_t)(max_k > 0 ? max_k : 1) + 63) / 64 * 64;
     if (split > cap) split = cap < 64 ? 64 : cap;

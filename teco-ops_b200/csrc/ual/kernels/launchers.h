@@ -91,7 +91,7 @@ struct DecodeParams {
 };
 
 bool decode_supported(int head_dim, int block_size, int group);
-// cache_fp8: an e4m3 cache (its CTAs move half the bytes per token, so splits are longer)
+// cache_fp8: an e4m3 cache (with a GQA group above 8 its splits are longer)
 void decode_plan(int num_sms, int batch, int kv_heads, int group, int max_k, int *split_tokens,
                  int *max_splits, bool cache_fp8 = false);
 size_t decode_workspace_bytes(int batch, int num_heads, int head_dim, int max_splits);

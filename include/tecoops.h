@@ -11,9 +11,11 @@
  * All data pointers are caller-owned DEVICE memory.  Every operator call is
  * asynchronous on the handle's stream and never synchronises the host.
  *
- * Symbols of the reference's other operators (rms_norm, causal_conv1d, ...)
- * are exported so that a program linking the reference library still links,
- * but they return TECOOPS_STATUS_NOT_SUPPORTED (they are not on this path).
+ * rms_norm (with the fused residual add), the step before the QKV projection in
+ * the same decoder layer, is implemented.  The reference's other operators
+ * (causal_conv1d, reduce_variance, flatten_rays, morton3D_invert) are exported so
+ * that a program linking the reference library still links, but they return
+ * TECOOPS_STATUS_NOT_SUPPORTED (they are not on this path).
  */
 #ifndef TECOOPS_B200_INCLUDE_TECOOPS_H_
 #define TECOOPS_B200_INCLUDE_TECOOPS_H_
@@ -285,17 +287,22 @@ tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(tecoopsHandle_t handle,
 
 /*
  * Extension with no counterpart in the reference: the split-KV decode of
- * tecoopsFlashAttention (every q_len 0 or 1) for callers that cannot allocate
- * device memory, such as an engine plugin that is handed only its input and
- * output buffers, or a server whose memory planner forbids allocations after
- * start-up.  It allocates nothing: the split scratch is a static 16 MiB device
- * array inside the library (held by every GPU that loads the library until
- * exit); shapes whose split plan needs more than 16 MiB are rejected with
- * TECOOPS_STATUS_NOT_SUPPORTED.  The first call on a device looks up the
- * array's device address, so make it before any stream capture.  All calls
- * share the array: calls that overlap on the GPU race and must be serialised.
- * Arguments as tecoopsFlashAttention (max_seqlen_q is implicitly 1, no
- * workspace); results are identical to it for the same inputs.
+ * tecoopsFlashAttention for callers that cannot allocate device memory, such as an
+ * engine plugin that is handed only its input and output buffers, or a server
+ * whose memory planner forbids allocations after start-up.  It allocates nothing:
+ * the split scratch is a static 16 MiB device array inside the library (minus 256
+ * bytes for its error word); shapes whose split plan needs more are rejected with
+ * TECOOPS_STATUS_NOT_SUPPORTED.  A GPU holds the array from the first call on that
+ * device (CUDA loads the library's device code lazily) until the process exits, so
+ * make one warm-up call per device at start-up, before carving up the memory pool
+ * and before any stream capture; that first call also looks up the array's device
+ * address.  All calls share the array: calls that overlap on the GPU race and must
+ * be serialised.  Preconditions: the calling thread's current device is the
+ * handle's; q has at most one row per sequence (BAD_PARAM otherwise) and every
+ * q_seq_lens entry is 0 or 1 (a larger one is reported as 0x1400 by
+ * tecoopsGetDeviceErrorStatus, which also reports waits that gave up).
+ * Arguments as tecoopsFlashAttention (max_seqlen_q is implicitly 1, no workspace);
+ * results are identical to it for the same inputs.
  */
 tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(tecoopsHandle_t handle, int max_seqlen_k,
                                                    const int *q_seq_lens, const int *kv_seq_lens,
@@ -311,12 +318,34 @@ tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(tecoopsHandle_t handle, int m
                                                    void *oData);
 
 /*
- * Extension: status of the last device-side check of this handle's stream
- * (bounded waits that gave up).  Synchronises the handle's stream.
- * Returns TECOOPS_STATUS_INTERNAL_ERROR if a kernel reported an error since the
- * previous call (and clears it), TECOOPS_STATUS_SUCCESS otherwise.
+ * Extension: status of the last device-side checks of this handle's stream.
+ * Synchronises the handle's stream.  Returns TECOOPS_STATUS_INTERNAL_ERROR if a
+ * kernel reported an error since the previous call (and clears it),
+ * TECOOPS_STATUS_SUCCESS otherwise; *error_code receives the first code found:
+ *   0x1nn-0xann  tcgen05 prefill: a bounded wait gave up (site in the high byte)
+ *   0x11nn       split-KV decode: the producer's wait for a free ring stage gave up
+ *   0x12nn       split-KV decode: a consumer's wait for a loaded chunk gave up
+ *   0x1300       split-KV decode: a kv_seq_lens entry exceeds max_seqlen_k (the keys
+ *                past the planned splits were not attended)
+ *   0x1400       split-KV decode: a q_seq_lens entry exceeds 1 (only the sequence's
+ *                first query row was computed)
+ * Reads the handle's own error word and, on the handle's device, the one of
+ * tecoopsFlashAttentionDecodeNoAlloc.
  */
 tecoopsStatus_t tecoopsGetDeviceErrorStatus(tecoopsHandle_t handle, int *error_code);
+
+/*
+ * Extension for tests of the failure path: sets the limit of every bounded device
+ * wait of the split-KV decode kernel launched through this handle (default
+ * 2,000,000,000 ns; 0 is BAD_PARAM).  stall_test != 0 makes the first ring wait of
+ * each consumer warp wait on a barrier that nothing completes, so that the wait runs
+ * out after limit_ns, records its site (0x12nn), and the kernel drains its copies
+ * and returns; the host then reads the code with tecoopsGetDeviceErrorStatus.
+ * Nothing faults, traps or waits without a bound.  stall_test = 0 restores normal
+ * operation.
+ */
+tecoopsStatus_t tecoopsSetDeviceWaitLimit(tecoopsHandle_t handle, unsigned long long limit_ns,
+                                          int stall_test);
 
 /*
  * rms_norm — RMSNorm, optionally fused with the residual add (the step before the

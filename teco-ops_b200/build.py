@@ -110,14 +110,24 @@ def build_oracle() -> str:
 
 def build_plugin() -> str:
     srcs = sorted(glob.glob(os.path.join(CSRC, "plugin", "**", "*.cc"), recursive=True))
+    cus = sorted(glob.glob(os.path.join(CSRC, "plugin", "**", "*.cu"), recursive=True))
     if not srcs:
         return ""
-    deps = srcs + _headers() + [LIB]
+    pinc = "-I" + os.path.join(CSRC, "plugin")
+    os.makedirs(BUILD, exist_ok=True)
+    objs = []
+    for cu in cus:   # the plugins' own small kernels (sm_100a)
+        obj = os.path.join(BUILD, "plugin_" + os.path.basename(cu) + ".o")
+        objs.append(obj)
+        if _stale(obj, [cu] + _headers()):
+            _run([NVCC, *ARCH, "-lineinfo", "-std=c++17", "-O3", "-Xcompiler", "-fPIC", *INCS,
+                  pinc, "-c", cu, "-o", obj])
+    deps = srcs + objs + _headers() + [LIB]
     if _stale(PLUGIN, deps):
-        _run(["g++", "-std=c++17", "-O2", "-shared", "-fPIC", *INCS,
-              "-I" + os.path.join(CSRC, "plugin"), "-I" + CUDA_INC, "-o", PLUGIN, *srcs,
-              "-L" + OUT, "-lteco_ops", "-L/usr/local/cuda/lib64", "-lcudart_static", "-ldl",
-              "-lrt", "-lpthread", "-Wl,-rpath,$ORIGIN", "-Wl,--no-undefined"])
+        _run(["g++", "-std=c++17", "-O2", "-shared", "-fPIC", *INCS, pinc, "-I" + CUDA_INC,
+              "-o", PLUGIN, *srcs, *objs, "-L" + OUT, "-lteco_ops", "-L/usr/local/cuda/lib64",
+              "-lcudart_static", "-ldl", "-lrt", "-lpthread", "-Wl,-rpath,$ORIGIN",
+              "-Wl,--no-undefined"])
     return PLUGIN
 
 

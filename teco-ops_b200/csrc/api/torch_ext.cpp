@@ -27,6 +27,7 @@
 #include <torch/library.h>
 
 #include <array>
+#include <cstdint>
 #include <map>
 #include <utility>
 #include <vector>
@@ -38,20 +39,43 @@ namespace {
 // One handle per (host thread, device, CUDA stream): a handle owns device scratch
 // (split-KV partials, the prefill unit scheduler's counters) that concurrent launches
 // on different streams must not share -- the reference's rule of one handle per
-// thread or stream, kept for callers that switch PyTorch streams.
+// thread or stream, kept for callers that switch PyTorch streams.  A thread keeps at
+// most kMaxHandles of them: past that, the least recently used one is destroyed
+// (tecoopsDestroy frees its scratch; cudaFree waits for the kernels that use it), so
+// a caller cycling through many streams does not accumulate scratch.
+constexpr size_t kMaxHandles = 8;
+
+struct HandleEntry {
+    tecoopsHandle_t h = nullptr;
+    uint64_t last_use = 0;
+};
+
 tecoopsHandle_t handleFor(int device) {
-    thread_local std::map<std::pair<int, cudaStream_t>, tecoopsHandle_t> handles;
+    thread_local std::map<std::pair<int, cudaStream_t>, HandleEntry> handles;
+    thread_local uint64_t tick = 0;
     TORCH_CHECK(device >= 0, "tecoops: device index out of range");
     const cudaStream_t stream = at::cuda::getCurrentCUDAStream(device).stream();
-    tecoopsHandle_t &h = handles[{device, stream}];
-    if (h == nullptr) {
+    const auto key = std::make_pair(device, stream);
+    auto it = handles.find(key);
+    if (it == handles.end()) {
+        if (handles.size() >= kMaxHandles) {
+            auto lru = handles.begin();
+            for (auto j = handles.begin(); j != handles.end(); ++j)
+                if (j->second.last_use < lru->second.last_use) lru = j;
+            c10::cuda::CUDAGuard g(lru->first.first);
+            tecoopsDestroy(lru->second.h);
+            handles.erase(lru);
+        }
         c10::cuda::CUDAGuard g(device);
-        tecoopsStatus_t st = tecoopsCreate(&h);
+        HandleEntry e;
+        tecoopsStatus_t st = tecoopsCreate(&e.h);
         TORCH_CHECK(st == TECOOPS_STATUS_SUCCESS, "tecoopsCreate failed: ",
                     tecoopsGetErrorString(st));
-        tecoopsSetStream(h, stream);
+        tecoopsSetStream(e.h, stream);
+        it = handles.emplace(key, e).first;
     }
-    return h;
+    it->second.last_use = ++tick;
+    return it->second.h;
 }
 
 tecoopsDataType_t dtypeOf(const torch::Tensor &t) {

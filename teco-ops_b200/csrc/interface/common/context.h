@@ -25,6 +25,11 @@ struct tecoopsContext {
     // gives up; [1], [2] the prefill kernel's work-unit and finished-CTA counters (zero
     // between launches: the last CTA of each launch resets them)
     int *dev_error = nullptr;
+    // limit of every bounded device wait of the split-KV decode kernel, and the test
+    // switch that makes its first ring wait wait on a barrier nothing completes
+    // (tecoopsSetDeviceWaitLimit)
+    unsigned long long wait_limit_ns = 2000000000ull;
+    int stall_test = 0;
 };
 
 struct tecoopsTensorStruct {
@@ -42,6 +47,9 @@ namespace interface {
 // device).  Returns nullptr on allocation failure.
 void *handleScratch(tecoopsContext *ctx, size_t bytes);
 int *handleErrorWord(tecoopsContext *ctx);
+// error word of tecoopsFlashAttentionDecodeNoAlloc on `device` (nullptr before its first
+// call there)
+int *noAllocErrorWord(int device);
 
 }  // namespace interface
 }  // namespace tecoops

@@ -210,16 +210,39 @@ tecoopsStatus_t tecoopsMemset(tecoopsHandle_t handle, void *x, const int value, 
 tecoopsStatus_t tecoopsGetDeviceErrorStatus(tecoopsHandle_t handle, int *error_code) {
     if (handle == nullptr) return TECOOPS_STATUS_NOT_INITIALIZED;
     if (error_code) *error_code = 0;
-    if (handle->dev_error == nullptr) return TECOOPS_STATUS_SUCCESS;
+    // the handle's own word, then the word of tecoopsFlashAttentionDecodeNoAlloc on the
+    // handle's device (that entry point allocates nothing, so its word is static)
+    int *words[2] = {handle->dev_error,
+                     tecoops::interface::noAllocErrorWord(handle->device)};
+    if (words[0] == nullptr && words[1] == nullptr) return TECOOPS_STATUS_SUCCESS;
     if (cudaStreamSynchronize(handle->stream) != cudaSuccess) return TECOOPS_STATUS_INTERNAL_ERROR;
-    int v = 0;
-    if (cudaMemcpy(&v, handle->dev_error, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
-        return TECOOPS_STATUS_INTERNAL_ERROR;
-    if (error_code) *error_code = v;
-    if (v != 0) {
-        cudaMemset(handle->dev_error, 0, sizeof(int));
-        return TECOOPS_STATUS_INTERNAL_ERROR;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != handle->device) cudaSetDevice(handle->device);
+    tecoopsStatus_t st = TECOOPS_STATUS_SUCCESS;
+    for (int *w : words) {
+        if (w == nullptr) continue;
+        int v = 0;
+        if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+            st = TECOOPS_STATUS_INTERNAL_ERROR;
+            break;
+        }
+        if (v != 0) {
+            cudaMemset(w, 0, sizeof(int));
+            if (st == TECOOPS_STATUS_SUCCESS && error_code) *error_code = v;
+            st = TECOOPS_STATUS_INTERNAL_ERROR;
+        }
     }
+    if (prev >= 0 && prev != handle->device) cudaSetDevice(prev);
+    return st;
+}
+
+tecoopsStatus_t tecoopsSetDeviceWaitLimit(tecoopsHandle_t handle, unsigned long long limit_ns,
+                                          int stall_test) {
+    if (handle == nullptr) return TECOOPS_STATUS_NOT_INITIALIZED;
+    if (limit_ns == 0) return TECOOPS_STATUS_BAD_PARAM;
+    handle->wait_limit_ns = limit_ns;
+    handle->stall_test = stall_test != 0 ? 1 : 0;
     return TECOOPS_STATUS_SUCCESS;
 }
 

@@ -113,6 +113,8 @@ static void fillArgs(FlashAttentionArgs &a, tecoopsHandle_t handle, int max_seql
     a.cache_fp8 = 0;
     a.k_scale = 1.f;
     a.v_scale = 1.f;
+    a.wait_limit_ns = handle->wait_limit_ns;
+    a.stall_test = handle->stall_test;
 }
 
 extern "C" tecoopsStatus_t tecoopsGetFlashAttentionWorkspaceSize(

@@ -10,19 +10,28 @@
 // to the handle's lazily grown scratch, and that fallback calls cudaMalloc.
 //
 // This entry point runs the same split-KV decode kernels with the same split
-// plan.  Its scratch (the per-split partial outputs and log-sum-exp values) lives
-// in a file-scope __device__ array of kNoAllocScratchBytes (16 MiB).  Every GPU
-// that loads this library holds that array until the process exits.
+// plan.  Its scratch lives in a file-scope __device__ array of
+// kNoAllocScratchBytes (16 MiB): the first 256 bytes hold the error word that the
+// kernels set when a bounded wait gives up or a length breaks the decode
+// preconditions, the rest the per-split partial outputs and log-sum-exp values.
+// A GPU holds the array from the moment this library's device code is loaded on
+// it until the process exits.  With CUDA's lazy module loading (the default since
+// CUDA 12.2) that moment is the first call of this entry point on the device, so
+// the 16 MiB are reserved by that call: make one warm-up call per device at
+// start-up, before the caller carves up its memory pool and before any stream
+// capture.
 //
 // Host code cannot use the array's name as a device address: in host code the
 // symbol is only a stand-in.  So the array's device address is looked up with
 // cudaGetSymbolAddress, once per device with that device current, on the first
-// call made on that device.  Make that first call before any stream capture.
+// call made on that device.
 //
 // All calls share the one array, and it keeps the contents of the last call.
-// Nothing in it needs to start at zero: every partial is written before it is
-// read within the same call.  Calls that overlap on the GPU (for example on two
-// streams of one device at once) race on the array; serialise them.
+// The partials need no clearing: every partial is written before it is read
+// within the same call.  The error word starts at zero (static device memory is
+// zero-initialised) and tecoopsGetDeviceErrorStatus clears it after reporting it.
+// Calls that overlap on the GPU (for example on two streams of one device at
+// once) race on the array; serialise them.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -36,6 +45,7 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 16u << 20;   // 16 MiB per device
+constexpr size_t kErrorBytes = 256;                   // error word, then the partials
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
@@ -62,6 +72,24 @@ void *scratchFor(int device) {
     }
     return g_scratch_ptr[device];
 }
+
+}  // namespace
+
+namespace tecoops {
+namespace interface {
+
+// The error word of this entry point on `device`, or nullptr if no call has set the
+// array up on that device yet (then no kernel of this entry point can have set it).
+int *noAllocErrorWord(int device) {
+    if (device < 0 || device >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    return static_cast<int *>(g_scratch_ptr[device]);
+}
+
+}  // namespace interface
+}  // namespace tecoops
+
+namespace {
 
 bool packedDesc(const tecoopsTensorStruct *d) {
     int s = 1;
@@ -113,7 +141,14 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
                    head_dim, block_size);
         return TECOOPS_STATUS_NOT_SUPPORTED;
     }
-    if (q->dimA[0] == 0) return TECOOPS_STATUS_SUCCESS;
+    // decode precondition: at most one query row per sequence (every q_seq_lens[b] is 0
+    // or 1; a length above 1 is reported through the error word)
+    if (q->dimA[0] > batch) {
+        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: q has %d rows for %d sequences; decode "
+                   "takes at most one query row per sequence",
+                   q->dimA[0], batch);
+        return TECOOPS_STATUS_BAD_PARAM;
+    }
 
     tecoops::kern::DecodeParams p;
     p.q = qData;
@@ -138,7 +173,9 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
     p.scale_log2 = (float)(1.0 / std::sqrt((double)head_dim)) * 1.4426950408889634f;
     p.part_o = nullptr;
     p.part_lse = nullptr;
-    p.dev_error = nullptr;
+    p.dev_error = nullptr;   // set below to the array's error word
+    p.wait_limit_ns = handle->wait_limit_ns;
+    p.stall_test = handle->stall_test;
     p.window_left = -1;
     p.lse = nullptr;
     p.new_key = nullptr;
@@ -149,20 +186,27 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
     p.v_scale = 1.f;
     const size_t need =
         tecoops::kern::decode_workspace_bytes(batch, heads, head_dim, p.max_splits);
-    if (need > kNoAllocScratchBytes) {
+    if (need > kNoAllocScratchBytes - kErrorBytes) {
         TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: these shapes need %zu bytes of split "
                    "scratch; the static scratch holds %zu bytes (16 MiB). Use "
                    "tecoopsFlashAttention with a workspace instead.",
                    need, kNoAllocScratchBytes);
         return TECOOPS_STATUS_NOT_SUPPORTED;
     }
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess) return TECOOPS_STATUS_INTERNAL_ERROR;
+    if (device != handle->device) {
+        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: the current device %d is not the "
+                   "handle's device %d",
+                   device, handle->device);
+        return TECOOPS_STATUS_BAD_PARAM;
+    }
+    unsigned char *scratch = static_cast<unsigned char *>(scratchFor(device));
+    if (scratch == nullptr) return TECOOPS_STATUS_INTERNAL_ERROR;
+    p.dev_error = reinterpret_cast<int *>(scratch);
     if (p.max_splits > 1) {
-        int device = -1;
-        if (cudaGetDevice(&device) != cudaSuccess) return TECOOPS_STATUS_INTERNAL_ERROR;
-        void *scratch = scratchFor(device);   // the current device's copy of the array
-        if (scratch == nullptr) return TECOOPS_STATUS_INTERNAL_ERROR;
         const size_t recs = (size_t)batch * heads * p.max_splits;
-        p.part_o = static_cast<float *>(scratch);
+        p.part_o = reinterpret_cast<float *>(scratch + kErrorBytes);
         p.part_lse = p.part_o + recs * head_dim;
     }
     const cudaError_t e =

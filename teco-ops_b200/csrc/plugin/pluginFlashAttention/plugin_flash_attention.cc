@@ -7,11 +7,16 @@
 //   output  [total, Hq, D] (the shape of q)
 // Two reference bugs are fixed here:
 //   * the reference passes cu_seqlens_q where tecoopsFlashAttention expects
-//     per-sequence lengths; this plugin converts the offsets to lengths (the host
-//     round trip the reference's torch binding also makes) into a device buffer
-//     owned by the plugin instance;
+//     per-sequence lengths; this plugin converts the offsets to lengths with a tiny
+//     kernel on the engine's stream (seq_lens.cu) into a device buffer owned by the
+//     plugin instance;
 //   * the reference builds the block-table descriptor from an empty shape; this one
 //     reads the block_table input's shape.
+// Enqueue never waits for the GPU: no host copy of the offsets and no stream
+// synchronisation.  The instance keeps one tecoops handle (and with it the split-KV
+// scratch and error word) for all its Enqueue calls, where the reference creates and
+// destroys a handle per call; the lengths buffer and the handle's scratch are
+// (re)allocated only when a call needs more than any earlier one.
 // The dtype of the descriptors follows the element type the engine declares through
 // the "dtype" attribute (TECOOPS_DATA_HALF by default, as in the reference).
 #include <plugin/register_op.h>
@@ -21,6 +26,7 @@
 #include <string>
 #include <vector>
 
+#include "pluginFlashAttention/seq_lens.h"
 #include "tecoops.h"
 
 namespace TECO_INFER {
@@ -40,6 +46,7 @@ TVM_REGISTER_NODE_TYPE(plugin_flash_attentionAttrs);
 class PluginFlashAttentionImpl : public AbstractPluginOp {
  public:
     ~PluginFlashAttentionImpl() override {
+        if (handle_) tecoopsDestroy(handle_);
         if (q_lens_dev_) cudaFree(q_lens_dev_);
     }
 
@@ -75,57 +82,58 @@ class PluginFlashAttentionImpl : public AbstractPluginOp {
         const int batch = bt_shape[0];
         cudaStream_t stream = ctx->GetStream();
 
-        // offsets -> lengths
-        std::vector<int> cu(batch + 1), lens(batch);
-        cudaMemcpyAsync(cu.data(), cu_seqlens_q, sizeof(int) * (batch + 1), cudaMemcpyDeviceToHost,
-                        stream);
-        cudaStreamSynchronize(stream);
-        for (int i = 0; i < batch; ++i) lens[i] = cu[i + 1] - cu[i];
+        if (handle_ == nullptr && tecoopsCreate(&handle_) != TECOOPS_STATUS_SUCCESS) {
+            handle_ = nullptr;
+            throw std::runtime_error("plugin_flash_attention: tecoopsCreate failed");
+        }
+        tecoopsSetStream(handle_, stream);
         if (q_lens_cap_ < batch) {
-            if (q_lens_dev_) cudaFree(q_lens_dev_);
+            if (q_lens_dev_) cudaFree(q_lens_dev_);   // waits for the calls that used it
             q_lens_dev_ = nullptr;
+            q_lens_cap_ = 0;
             if (cudaMalloc(&q_lens_dev_, sizeof(int) * batch) != cudaSuccess)
                 throw std::runtime_error("plugin_flash_attention: allocation failed");
             q_lens_cap_ = batch;
         }
-        cudaMemcpyAsync(q_lens_dev_, lens.data(), sizeof(int) * batch, cudaMemcpyHostToDevice,
-                        stream);
+        // offsets -> lengths on the engine's stream, ahead of the attention kernels
+        if (launchOffsetsToLengths(static_cast<const int *>(cu_seqlens_q), batch, q_lens_dev_,
+                                   stream) != cudaSuccess)
+            throw std::runtime_error("plugin_flash_attention: lengths kernel launch failed");
 
-        tecoopsHandle_t handle;
-        tecoopsCreate(&handle);
-        tecoopsSetStream(handle, stream);
         auto make_desc = [&](tecoopsTensorDescriptor_t &d, tecoopsDataType_t dt,
                              const std::vector<int> &shape) {
-            tecoopsCreateTensorDescriptor(&d);
+            if (d == nullptr) tecoopsCreateTensorDescriptor(&d);
             tecoopsSetTensorNdDescriptor(d, dt, (int)shape.size(), shape.data(), nullptr);
         };
         const tecoopsDataType_t dt = static_cast<tecoopsDataType_t>(dtype);
-        tecoopsTensorDescriptor_t btD, qD, kD, vD, oD;
-        make_desc(btD, TECOOPS_DATA_INT32, bt_shape);
-        make_desc(qD, dt, q_shape);
-        make_desc(kD, dt, k_shape);
-        make_desc(vD, dt, k_shape);
-        make_desc(oD, dt, q_shape);
+        Descs &D = descs_;
+        make_desc(D.bt, TECOOPS_DATA_INT32, bt_shape);
+        make_desc(D.q, dt, q_shape);
+        make_desc(D.k, dt, k_shape);
+        make_desc(D.v, dt, k_shape);
+        make_desc(D.o, dt, q_shape);
         const tecoopsStatus_t st = tecoopsFlashAttention(
-            handle, (int)max_seqlen_q, (int)max_seqlen_k, (int)max_block_num, q_lens_dev_,
-            static_cast<const int *>(seqused_k), btD, block_table, qD, q, kD, k_cache, vD, v_cache,
-            oD, out, nullptr);
-        // the lengths buffer must stay valid until the kernels that read it ran
-        cudaStreamSynchronize(stream);
-        tecoopsDestroyTensorDescriptor(btD);
-        tecoopsDestroyTensorDescriptor(qD);
-        tecoopsDestroyTensorDescriptor(kD);
-        tecoopsDestroyTensorDescriptor(vD);
-        tecoopsDestroyTensorDescriptor(oD);
-        tecoopsDestroy(handle);
+            handle_, (int)max_seqlen_q, (int)max_seqlen_k, (int)max_block_num, q_lens_dev_,
+            static_cast<const int *>(seqused_k), D.bt, block_table, D.q, q, D.k, k_cache, D.v,
+            v_cache, D.o, out, nullptr);
         if (st != TECOOPS_STATUS_SUCCESS)
             throw std::runtime_error(std::string("plugin_flash_attention: ") +
                                      tecoopsGetErrorString(st));
     }
 
  private:
+    struct Descs {
+        tecoopsTensorDescriptor_t bt = nullptr, q = nullptr, k = nullptr, v = nullptr,
+                                  o = nullptr;
+        ~Descs() {
+            for (tecoopsTensorDescriptor_t d : {bt, q, k, v, o})
+                if (d) tecoopsDestroyTensorDescriptor(d);
+        }
+    };
+    tecoopsHandle_t handle_ = nullptr;   // created on the device current at the first call
     int *q_lens_dev_ = nullptr;
     int q_lens_cap_ = 0;
+    Descs descs_;
 };
 
 REGISTER_PLUGIN_OP_IMPL(plugin_flash_attention, PluginFlashAttentionImpl)

@@ -5,6 +5,9 @@
 
 #include <cstring>
 #include <exception>
+#include <map>
+#include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -75,13 +78,13 @@ int teco_plugin_infer(const char *op, int n_in, const int *ranks, const int *dim
     }
 }
 
-// Enqueue with named inputs on `stream` (a cudaStream_t).
-int teco_plugin_enqueue(const char *op, int n_in, const char *const *in_names,
-                        void *const *in_ptrs, const int *ranks, const int *dims_flat, int n_out,
-                        void *const *out_ptrs, int n_attr, const char *const *attr_names,
-                        const double *attr_vals, void *stream) {
-    auto it = TECO_INFER::plugin_impls().find(op);
-    if (it == TECO_INFER::plugin_impls().end()) return -1;
+namespace {
+
+// Enqueue of `impl` with named inputs on `stream` (a cudaStream_t).
+int enqueue_impl(TECO_INFER::AbstractPluginOp &impl, int n_in, const char *const *in_names,
+                 void *const *in_ptrs, const int *ranks, const int *dims_flat, int n_out,
+                 void *const *out_ptrs, int n_attr, const char *const *attr_names,
+                 const double *attr_vals, void *stream) {
     try {
         auto ctx = std::make_shared<TECO_INFER::ComputeContext>();
         auto shapes = make_shapes(n_in, ranks, dims_flat);
@@ -93,13 +96,63 @@ int teco_plugin_enqueue(const char *op, int n_in, const char *const *in_names,
         ctx->outputs.assign(out_ptrs, out_ptrs + n_out);
         ctx->attr = make_attr(n_attr, attr_names, attr_vals);
         ctx->stream = static_cast<cudaStream_t>(stream);
-        auto impl = it->second();
-        impl->Enqueue(ctx);
+        impl.Enqueue(ctx);
         return 0;
     } catch (const std::exception &e) {
         g_last_error = e.what();
         return -2;
     }
+}
+
+// op instances that live across Enqueue calls, as an engine keeps one per graph node
+std::mutex g_instances_mutex;
+std::map<int, std::unique_ptr<TECO_INFER::AbstractPluginOp>> g_instances;
+int g_next_instance = 1;
+
+}  // namespace
+
+// One-shot Enqueue: a fresh instance of `op` for this call only (destroyed after it).
+int teco_plugin_enqueue(const char *op, int n_in, const char *const *in_names,
+                        void *const *in_ptrs, const int *ranks, const int *dims_flat, int n_out,
+                        void *const *out_ptrs, int n_attr, const char *const *attr_names,
+                        const double *attr_vals, void *stream) {
+    auto it = TECO_INFER::plugin_impls().find(op);
+    if (it == TECO_INFER::plugin_impls().end()) return -1;
+    auto impl = it->second();
+    return enqueue_impl(*impl, n_in, in_names, in_ptrs, ranks, dims_flat, n_out, out_ptrs,
+                        n_attr, attr_names, attr_vals, stream);
+}
+
+// A persistent instance of `op`: returns its id (> 0), or -1 for an unknown op.
+int teco_plugin_create(const char *op) {
+    auto it = TECO_INFER::plugin_impls().find(op);
+    if (it == TECO_INFER::plugin_impls().end()) return -1;
+    std::lock_guard<std::mutex> lock(g_instances_mutex);
+    const int id = g_next_instance++;
+    g_instances[id] = it->second();
+    return id;
+}
+
+// Enqueue on a persistent instance (the call returns as soon as the work is enqueued).
+int teco_plugin_enqueue_instance(int id, int n_in, const char *const *in_names,
+                                 void *const *in_ptrs, const int *ranks, const int *dims_flat,
+                                 int n_out, void *const *out_ptrs, int n_attr,
+                                 const char *const *attr_names, const double *attr_vals,
+                                 void *stream) {
+    TECO_INFER::AbstractPluginOp *impl = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_instances_mutex);
+        auto it = g_instances.find(id);
+        if (it == g_instances.end()) return -1;
+        impl = it->second.get();
+    }
+    return enqueue_impl(*impl, n_in, in_names, in_ptrs, ranks, dims_flat, n_out, out_ptrs,
+                        n_attr, attr_names, attr_vals, stream);
+}
+
+int teco_plugin_destroy(int id) {
+    std::lock_guard<std::mutex> lock(g_instances_mutex);
+    return g_instances.erase(id) == 1 ? 0 : -1;
 }
 
 }  // extern "C"

@@ -54,6 +54,9 @@ struct FlashAttentionArgs {
     int cache_fp8;
     float k_scale;
     float v_scale;
+    // bounded device waits of the decode kernel (tecoopsSetDeviceWaitLimit)
+    unsigned long long wait_limit_ns;
+    int stall_test;
 };
 
 // Branch selection input (reference FlashAttentionPatchArgs).

@@ -72,6 +72,9 @@ namespace kern {
 namespace {
 
 constexpr int kChunk = 16;        // tokens per ring stage (one MMA n-tile pair)
+// error-word codes of caller errors the kernel detects (bounded waits use 0x11xx, 0x12xx)
+constexpr int kErrKvBeyondPlan = 0x1300;   // kv_seq_lens[b] above max_seqlen_k: keys cut
+constexpr int kErrQLenAboveOne = 0x1400;   // q_seq_lens[b] > 1: only the first row computed
 constexpr int kConsumers = 4;
 constexpr int kThreads = 32 * (kConsumers + 1);
 
@@ -143,18 +146,6 @@ __device__ __forceinline__ uint32_t swz128(int r, int ch) {
 }  // namespace
 
 // FP8: 2 CTAs per SM (the raw key/value words and their conversions need registers)
-#ifdef TECOOPS_DECODE_TRACE
-// Development-only timeline capture (not built into the library): per-chunk clock64()
-// stamps of the consumers and producer of CTAs (0, 0, z < 64).
-__device__ long long g_decode_trace[64 * 4 * 16 * 8];
-__device__ long long g_decode_trace_p[64 * 64];
-extern "C" int tecoops_decode_trace_read_p(long long *host, size_t n) {
-    return (int)cudaMemcpyFromSymbol(host, g_decode_trace_p, n * sizeof(long long));
-}
-extern "C" int tecoops_decode_trace_read(long long *host, size_t n) {
-    return (int)cudaMemcpyFromSymbol(host, g_decode_trace, n * sizeof(long long));
-}
-#endif
 // TP: the transposed form (GQA group of at most 8 heads)
 template <typename T, int D, bool FP8, bool TP>
 __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
@@ -164,7 +155,9 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
     extern __shared__ uint8_t smem_raw[];
     using Sm = DecodeSmem<D, FP8, TP>;
     constexpr int kStages = Sm::kStages;
-    __shared__ __align__(8) uint64_t bars[2 * kStages];
+    // ring FULL / EMPTY barriers, then one barrier that nothing ever completes (the
+    // target of the give-up test, DecodeParams::stall_test)
+    __shared__ __align__(8) uint64_t bars[2 * kStages + 1];
     __shared__ int abort_flag;
     using MT = typename std::conditional<FP8, __half, T>::type;   // MMA operand type
 
@@ -183,7 +176,14 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
     const int kv_lo = p.window_left >= 0 ? max(0, kv_len - 1 - p.window_left) : 0;
     const int kv_base = kv_lo & ~(kChunk - 1);
     const int kv_begin = kv_base + split * p.split_tokens;
-    const int n_split_b = (kv_len - kv_base + p.split_tokens - 1) / p.split_tokens;
+    // the grid has max_splits splits (planned from max_seqlen_k) and the scratch holds
+    // max_splits records per row: a kv_len beyond that plan is cut to it and reported
+    const int n_split_need = (kv_len - kv_base + p.split_tokens - 1) / p.split_tokens;
+    const int n_split_b = min(n_split_need, p.max_splits);
+    if (split == 0 && blockIdx.y == 0 && threadIdx.x == 0 && p.dev_error != nullptr) {
+        if (n_split_need > p.max_splits) atomicCAS(p.dev_error, 0, kErrKvBeyondPlan);
+        if (q_len > 1) atomicCAS(p.dev_error, 0, kErrQLenAboveOne);
+    }
     if (kv_begin >= kv_len && !(split == 0 && kv_len - kv_base <= 0)) return;
     const int kv_end = min(kv_len, kv_begin + p.split_tokens);
     const int qrow = warp_seq_start(p.q_seq_lens, b);   // q_len == 1 on this path
@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
             mbar_init(FULL(s), 1);
             mbar_init(EMPTY(s), 1);
         }
+        mbar_init(bar0 + 16u * kStages, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -270,11 +271,8 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                     const int st = ci % kStages;
                     if (ci >= kStages)
                         lok = mbar_wait_bounded(EMPTY(st), ((ci / kStages) - 1) & 1, abortp,
-                                                p.dev_error, 0x1100 + (ci & 0xff));
-#ifdef TECOOPS_DECODE_TRACE
-                    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z < 64 && ci < 64)
-                        g_decode_trace_p[blockIdx.z * 64 + ci] = clock64();
-#endif
+                                                p.dev_error, 0x1100 + (ci & 0xff),
+                                                p.wait_limit_ns);
                     if (lok) {
                         mbar_arrive_expect_tx(FULL(st), Sm::kStageBytes);
                         const uint32_t kd = sbase + st * Sm::kStageBytes;
@@ -335,23 +333,17 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
         const float sl2 = p.scale_log2;
         const int mi = lane >> 3;   // ldmatrix matrix index of this lane's address
         const int ri = lane & 7;
-#ifdef TECOOPS_DECODE_TRACE
-        const bool trc = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z < 64 && lane == 0;
-        long long *trp = g_decode_trace + ((blockIdx.z * 4 + warp) * 16) * 8;
-        long long tprev = clock64();
-#define DTRACE(i, e) do { if (trc && (i) < 16) trp[(i) * 8 + (e)] = clock64(); } while (0)
-#define DTRACE_DEP(x) do { if (trc && (x) == 12345.f) trp[0] = 0; } while (0)   // orders the stamp
-#else
-#define DTRACE(i, e) do {} while (0)
-#define DTRACE_DEP(x) do {} while (0)
-#endif
         for (int ci = warp; ci < nch; ci += kConsumers) {
             const int st = ci % kStages;
-            DTRACE(ci / 4, 0);
-            if (!__all_sync(0xffffffffu, mbar_wait_bounded(FULL(st), (ci / kStages) & 1, abortp,
-                                                           p.dev_error, 0x1200 + (ci & 0xff))))
+            // (stall_test: the first wait of each consumer targets the barrier nothing
+            // completes, so it runs out and takes the abort path below)
+            const bool stall = p.stall_test && ci == warp;
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait_bounded(stall ? bar0 + 16u * kStages : FULL(st),
+                                              stall ? 0u : (ci / kStages) & 1, abortp,
+                                              p.dev_error, 0x1200 + (ci & 0xff),
+                                              p.wait_limit_ns)))
                 break;
-            DTRACE(ci / 4, 1);
             const int tok0 = kv_begin + ci * kChunk;
             const int nv = kv_end - tok0;   // tokens of this chunk before kv_end
             const int nlo = kv_lo - tok0;   // tokens of this chunk before the window
@@ -609,8 +601,6 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                     mx[e >> 1] = fmaxf(mx[e >> 1], x);
                 }
             }
-            DTRACE_DEP(mx[0]);
-            DTRACE(ci / 4, 2);
             float mu[2], alpha[2];
             bool grow = false;
 #pragma unroll
@@ -644,8 +634,6 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                     o[n][3] *= alpha[1];
                 }
             }
-            DTRACE_DEP(alpha[0]);
-            DTRACE(ci / 4, 3);
             uint32_t pa[4];
             pa[0] = Elem<MT>::pack2(s[0][0], s[0][1]);
             pa[1] = Elem<MT>::pack2(s[0][2], s[0][3]);
@@ -678,8 +666,6 @@ __global__ void __launch_bounds__(kThreads, FP8 && !TP ? 2 : 3)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(EMPTY(st));
             }
-            DTRACE_DEP(o[0][0]);
-            DTRACE(ci / 4, 4);
         }
         if constexpr (TP) {   // partial sums of heads 2c, 2c+1 over the 8 token lanes
 #pragma unroll
@@ -784,7 +770,8 @@ __global__ void __launch_bounds__(128) fa_decode_merge_kernel(DecodeParams p) {
     const int q_len = __ldg(p.q_seq_lens + b);
     const int kv_len = __ldg(p.kv_seq_lens + b);
     const int kv_lo = p.window_left >= 0 ? max(0, kv_len - 1 - p.window_left) : 0;
-    const int ns = (kv_len - (kv_lo & ~15) + p.split_tokens - 1) / p.split_tokens;
+    const int ns =
+        min((kv_len - (kv_lo & ~15) + p.split_tokens - 1) / p.split_tokens, p.max_splits);
     if (q_len <= 0 || ns <= 1) return;
     const int qrow = warp_seq_start(p.q_seq_lens, b);
     if (qrow >= p.total_q) return;

@@ -115,21 +115,6 @@ __device__ __forceinline__ void st_global_v8(void *ptr, const uint32_t *w) {
                  : "memory");
 }
 
-#ifdef TECOOPS_PREFILL_TRACE
-// Development-only timeline capture (not built into the library): per CTA, clock64()
-// stamps of the pipeline events, read back with tecoops_prefill_trace_read.
-__device__ long long g_prefill_trace[8192 * 128];
-#define PTRACE(slot, v)                                                                  \
-    do {                                                                                 \
-        const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
-        if (cta_ < 8192) g_prefill_trace[cta_ * 128 + (slot)] = (long long)(v);          \
-    } while (0)
-#else
-#define PTRACE(slot, v) \
-    do {                \
-    } while (0)
-#endif
-
 enum WaitSite : int {
     kSiteQ = 0x100, kSiteK = 0x200, kSiteV = 0x300, kSiteEmpty = 0x400, kSiteS = 0x500,
     kSiteP = 0x600, kSiteO = 0x700, kSiteDrain = 0x800, kSiteVz = 0x900, kSiteSched = 0xa00
@@ -230,19 +215,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     volatile int *abortp = &abort_flag;
-#ifdef TECOOPS_PREFILL_TRACE
-    if (threadIdx.x == 0) {
-        unsigned smid;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        PTRACE(0, globaltimer_ns());
-        PTRACE(1, smid);
-        PTRACE(2, clock64());
-    }
-#endif
-#define UTRACE(k, e, v) \
-    do {                \
-        if ((k) < 7) PTRACE(8 + 16 * (k) + (e), (v)); \
-    } while (0)
 
     // Work units, heaviest first: index = ((u_from_top * batch) + b) * units_per_row + hp.
     // CTA c starts on unit c; further units are handed out dynamically from
@@ -514,11 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 Unit u;
                 if (!decode_unit(e, u) || u.N == 0) continue;
                 const bool partial = u.N * kBN > u.S;
-                UTRACE(units, 0, clock64());
-                UTRACE(units, 7, u.N);
                 ok = mbar_wait_bounded(BAR(Q_FULL), units & 1, abortp, p.dev_error, kSiteQ) &&
                      wait_k(kt);
-                UTRACE(units, 1, clock64());
                 ++units;
                 if (!ok) break;
                 tc_fence_after();
@@ -555,8 +524,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = mbar_wait_bounded(BAR(O_FREE + X), (ounits[X] - 1) & 1, abortp,
                                                    p.dev_error, kSiteO);
                         if (!ok) break;
-                        if (X == 0 && j == u.J0) UTRACE(units - 1, 6, clock64());
-                        if (X == 0 && j + 1 == u.N) UTRACE(units - 1, 2, clock64());
                         tc_fence_after();
                         issue_pv(X, vj, j == u.J0);
                         if (j + 1 < n) {
@@ -621,9 +588,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                  : u.S - 1),
                                  u.S - 1);
             const int klo = kWindow ? max(0, u.off + qi - p.window_left) : 0;
-#ifdef TECOOPS_PREFILL_TRACE
-            long long tr_busy = 0, tr_wait = 0, tr_prev = clock64(), tr_s = 0;
-#endif
             float m_s = -INFINITY;   // running max, scaled (log2) units
             float l = 0.f;
             for (int j = u.J0; j < n; ++j) {
@@ -633,11 +597,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 ++scount;
-                if (warp == 2 && lane == 0 && j == u.J0) UTRACE(ocount, 3, clock64());
-#ifdef TECOOPS_PREFILL_TRACE
-                tr_s = clock64();
-                if (j > u.J0) tr_wait += tr_s - tr_prev;
-#endif
                 tc_fence_after();
                 const int kbase = j * kBN;
                 // columns c outside [nlo, nvalid) are masked (causal / window / kv_len tail)
@@ -697,10 +656,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(BAR(P_FULL + X));
-#ifdef TECOOPS_PREFILL_TRACE
-                tr_prev = clock64();
-                tr_busy += tr_prev - tr_s;
-#endif
             }
             if (!ok) break;
             // epilogue; then hand O_X back for the next unit's first PV
@@ -708,13 +663,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                            p.dev_error, kSiteO))) {
                 ok = false;
                 break;
-            }
-            if (warp == 2 && lane == 0) {
-                UTRACE(ocount, 4, clock64());
-#ifdef TECOOPS_PREFILL_TRACE
-                UTRACE(ocount, 8, tr_busy);
-                UTRACE(ocount, 9, tr_wait);
-#endif
             }
             ++ocount;
             tc_fence_after();
@@ -752,13 +700,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            if (warp == 2 && lane == 0) UTRACE(ocount - 1, 5, clock64());
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (threadIdx.x == 0) PTRACE(3, clock64());
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
@@ -772,12 +718,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 }
-
-#ifdef TECOOPS_PREFILL_TRACE
-extern "C" int tecoops_prefill_trace_read(long long *host, size_t n) {
-    return (int)cudaMemcpyFromSymbol(host, g_prefill_trace, n * sizeof(long long));
-}
-#endif
 
 // ---- host side ------------------------------------------------------------------------
 

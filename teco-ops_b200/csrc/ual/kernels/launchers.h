@@ -88,6 +88,9 @@ struct DecodeParams {
     int kv_layout;      // 0: [pages, Hkv, bs, D]; 1: [pages, bs, Hkv, D]
     int cache_fp8;      // e4m3 cache: K*k_scale folded into scale_log2, O *= v_scale
     float v_scale;
+    unsigned long long wait_limit_ns;   // limit of each bounded mbarrier wait
+    int stall_test;     // test of the give-up path: the first ring wait of each consumer
+                        // waits on a barrier that nothing completes
 };
 
 bool decode_supported(int head_dim, int block_size, int group);

@@ -84,6 +84,8 @@ static cudaError_t runDecode(const FlashAttentionArgs &a, cudaStream_t stream) {
     p.new_key = a.new_key;
     p.new_value = a.new_value;
     p.slot_mapping = a.slot_mapping;
+    p.wait_limit_ns = a.wait_limit_ns;
+    p.stall_test = a.stall_test;
     if (p.max_splits > 1) {
         const size_t need = kern::decode_workspace_bytes(p.batch, p.num_heads, p.head_dim,
                                                          p.max_splits);

@@ -31,7 +31,8 @@ EXPORTED = [
     "tecoopsGetTensor4dDescriptor", "tecoopsSetTensorNdDescriptor",
     "tecoopsGetTensorNdDescriptor", "tecoopsDestroyTensorDescriptor", "tecoopsMemset",
     "tecoopsReshapeAndCache", "tecoopsReshapeAndCacheEx", "tecoopsFlashAttention", "tecoopsGetFlashAttentionWorkspaceSize",
-    "tecoopsGetDeviceErrorStatus", "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlashAttentionEx",
+    "tecoopsGetDeviceErrorStatus", "tecoopsSetDeviceWaitLimit",
+    "tecoopsFlashAttentionDecodeNoAlloc", "tecoopsFlashAttentionEx",
     "tecoopsReshapeAndCacheFlashAttentionDecode", "tecoopsFlattenRays", "tecoopsReduceVariance",
     "tecoopsMorton3DInvert", "tecoopsRmsNorm", "tecoopsRmsNormEx", "tecoopsCausalConv1d",
 ]
@@ -89,6 +90,7 @@ def lib():
         "tecoopsGetFlashAttentionWorkspaceSize": [_vp, _i, _i, _vp, _vp, _vp,
                                                   ctypes.POINTER(ctypes.c_size_t)],
         "tecoopsGetDeviceErrorStatus": [_vp, ctypes.POINTER(_i)],
+        "tecoopsSetDeviceWaitLimit": [_vp, ctypes.c_ulonglong, _i],
         "tecoopsFlashAttentionDecodeNoAlloc": [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                                _vp, _vp, _vp, _vp],
         "tecoopsFlashAttentionEx": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
@@ -258,3 +260,9 @@ def device_error(handle: Handle):
     code = _i(0)
     st = lib().tecoopsGetDeviceErrorStatus(handle.h, ctypes.byref(code))
     return st, code.value
+
+
+def set_device_wait_limit(handle: Handle, limit_ns: int, stall_test: bool = False) -> int:
+    """Limit of the decode kernel's bounded waits; stall_test makes its first ring
+    wait target a barrier nothing completes (tests of the give-up path)."""
+    return lib().tecoopsSetDeviceWaitLimit(handle.h, int(limit_ns), 1 if stall_test else 0)

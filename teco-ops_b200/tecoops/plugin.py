@@ -76,3 +76,33 @@ def enqueue(op: str, inputs: dict, outputs, attrs: dict, stream: int = 0):
                                    len(outputs), out_ptrs, na, an, av, ctypes.c_void_p(stream))
     if st != 0:
         raise RuntimeError(f"{op}: enqueue failed ({st}): {lib().teco_plugin_last_error().decode()}")
+
+
+class Instance:
+    """A plugin op instance that lives across Enqueue calls, as an engine keeps one per
+    graph node (its device buffers and tecoops handle are reused)."""
+
+    def __init__(self, op: str):
+        self.id = lib().teco_plugin_create(op.encode())
+        if self.id < 0:
+            raise RuntimeError(f"{op}: unknown plugin op")
+        self.op = op
+
+    def enqueue(self, inputs: dict, outputs, attrs: dict, stream: int = 0):
+        names = list(inputs)
+        in_names = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        in_ptrs = (ctypes.c_void_p * len(names))(*[inputs[n][0] for n in names])
+        ranks, dims = _shapes([inputs[n][1] for n in names])
+        out_ptrs = (ctypes.c_void_p * len(outputs))(*outputs)
+        na, an, av = _attrs(attrs)
+        st = lib().teco_plugin_enqueue_instance(self.id, len(names), in_names, in_ptrs, ranks,
+                                                dims, len(outputs), out_ptrs, na, an, av,
+                                                ctypes.c_void_p(stream))
+        if st != 0:
+            raise RuntimeError(f"{self.op}: enqueue failed ({st}): "
+                               f"{lib().teco_plugin_last_error().decode()}")
+
+    def close(self):
+        if self.id > 0:
+            lib().teco_plugin_destroy(self.id)
+            self.id = -1

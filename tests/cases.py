@@ -5,13 +5,13 @@ Shapes follow the reference's own test cases:
   (512 tokens, H 8/4/2, D 128, 64 pages x 16, slot_mapping overwritten with
   0..T-1 as reshape_and_cache.cpp:77-84 does, caches zeroed) and
   python_api_test/test_reshape_and_cache.py:70-75 (same shapes), plus
-  BASELINE config 1 (random permutation slots with ~5% -1 padding, caches
+  the CPU-runnable fp16 pair (random permutation slots with ~5% -1 padding, caches
   pre-filled with a sentinel so untouched slots are checked too) and edge cases.
 * attention: test/zoo/teco/flash_attention/test_case/{0..5}.prototxt (block_size
   32, U(-1, 1) inputs, block tables drawn uniformly from [0, 255] — duplicates
   allowed), python_api_test/test_flash_attention.py:265-358 (prefill, decode,
   chunked, GQA, mixed; N(0, 1) inputs, 64-page pool, shuffled block tables),
-  BASELINE config 1 and block_size-16 / bf16 / head_dim-64 variants.
+  that pair's prefill and block_size-16 / bf16 / head_dim-64 variants.
 
 Inputs are regenerated bit-identically from (seed, shape) by oracle.seeded.
 """
@@ -42,7 +42,7 @@ RESHAPE_CASES = {
                       init="zeros", seed=102),
     "zoo_case2": dict(T=512, H=2, D=128, NB=64, bs=16, dtype="f16", slots="arange", pad=0.0,
                       init="zeros", seed=103),
-    # BASELINE config 1 (fp16, randperm(1024)[:256], ~5% -1)
+    # CPU-runnable fp16 pair: randperm(1024)[:256] slots, ~5% -1
     "cfg1_fp16": dict(T=256, H=8, D=128, NB=64, bs=16, dtype="f16", slots="perm", pad=0.05,
                       init="sentinel", seed=1),
     "cfg1_bf16": dict(T=256, H=8, D=128, NB=64, bs=16, dtype="bf16", slots="perm", pad=0.05,
@@ -119,7 +119,7 @@ ATTN_CASES = {
     "api_gqa_8q2kv_chunked": _fa([32], [64], 8, 2, 128, 32, 64, "f16", "normal", 31),
     "api_gqa_2q1kv_decode_2b": _fa([1, 1], [64, 128], 2, 1, 128, 32, 64, "f16", "normal", 32),
     "api_mix_decode_prefill": _fa([1, 32], [128, 64], 8, 4, 128, 32, 64, "f16", "normal", 33),
-    # BASELINE config 1 prefill (fp16, bs 16)
+    # CPU-runnable fp16 pair: causal prefill B 1, L 256, 8/8 heads, bs 16
     "cfg1_prefill": _fa([256], [256], 8, 8, 128, 16, 64, "f16", "normal", 4),
     # block_size 16 / bf16 / ragged variants on the B200 paths
     "bf16_bs16_varlen": _fa([200, 37, 513], [200, 300, 513], 32, 8, 128, 16, 160, "bf16", "normal", 40),

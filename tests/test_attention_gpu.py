@@ -71,7 +71,7 @@ def test_attention_deterministic():
 
 
 def _config2_inputs(seed=10):
-    """4 seqs, L ~ U{512..2048}, Hq 32, Hkv 8, D 128, bf16, bs 16,
+    """Llama-3-8B varlen prefill: 4 seqs, L ~ U{512..2048}, Hq 32, Hkv 8, D 128, bf16, bs 16,
     contiguous pages, K/V written by reshape_and_cache first."""
     g = torch.Generator(device="cpu").manual_seed(seed)
     lens = torch.randint(512, 2049, (4,), generator=g).tolist()
@@ -110,7 +110,7 @@ def test_config2_prefill_full_size():
 
 
 def test_config3_decode_full_size():
-    """64 seqs, context U{512..8192}, 40,000-page pool with a
+    """Llama-3-8B paged decode: 64 seqs, context U{512..8192}, 40,000-page pool with a
     random permutation, bs 16, Hq 32, Hkv 8, D 128, bf16."""
     from gpu_util import attention_capi, errors
     B, Hq, Hkv, D, bs, pool = 64, 32, 8, 128, 16, 40000
@@ -193,7 +193,7 @@ def test_kv_head_shards_reassemble(name, world):
 
 
 def test_config5_prefill_sampled_rows():
-    """BASELINE config 5 prefill (Hq 64, Hkv 8, 2 x 8192 causal) at full size; checked on
+    """Llama-3-70B prefill (Hq 64, Hkv 8, 2 x 8192 causal) at full size; checked on
     KV head 0's Q group for the last 256 rows of each sequence (they attend to all 8192
     keys; the oracle treats them as a chunked prefill of 256 rows over 8192 keys)."""
     from gpu_util import attention_capi, errors, reshape_capi
@@ -221,7 +221,7 @@ def test_config5_prefill_sampled_rows():
 
 
 def test_config5_decode_sampled_sequences():
-    """BASELINE config 5 decode (B 256, ctx U{1024..32768}, Hq 64, Hkv 8) at full size on a
+    """Llama-3-70B decode (B 256, ctx U{1024..32768}, Hq 64, Hkv 8) at full size on a
     270k-page pool; 16 sequences checked against the oracle on a compacted pool."""
     from gpu_util import attention_capi, errors
     B, Hq, Hkv, D, bs = 256, 64, 8, 128, 16

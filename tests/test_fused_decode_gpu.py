@@ -77,7 +77,7 @@ def test_fused_decode_padding_slot_leaves_cache():
 
 
 def test_fused_decode_config3_full_size():
-    """BASELINE config 3 step (64 new tokens, 40,000-page pool): fused == unfused."""
+    """Llama-3-8B paged decode step (64 new tokens, 40,000-page pool): fused == unfused."""
     from gpu_util import attention_capi, handle, reshape_capi
     from tecoops import capi
     B, Hq, Hkv, D, bs, pool = 64, 32, 8, 128, 16, 40000

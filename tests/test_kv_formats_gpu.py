@@ -208,7 +208,7 @@ def test_fp8_vllm_decode_step_round_trip():
 
 
 def test_fp8_prefill_config2_full_size():
-    """BASELINE config 2 shapes on an e4m3 cache (scale 1/64) through the tcgen05
+    """Llama-3-8B varlen prefill shapes on an e4m3 cache (scale 1/64) through the tcgen05
     prefill: tolerance against the oracle on the dequantised cache."""
     from gpu_util import errors
     from tecoops import capi

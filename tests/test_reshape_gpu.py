@@ -38,7 +38,7 @@ def test_reshape_bit_exact_vs_golden(golden, name):
                                            (4096, "scattered", 0.1), (65536, "scattered", 0.0),
                                            (65536, "sequential", 0.1)])
 def test_reshape_full_size_properties(T, layout, pad):
-    """BASELINE config 4 sizes (65,536-page cache, 2 GiB per cache): every valid
+    """Reshape-sweep sizes (65,536-page cache, 2 GiB per cache): every valid
     token's rows land bit-exactly at their slot and nothing else changes."""
     from gpu_util import reshape_capi
     H, D, NB, BS = 8, 128, 65536, 16

@@ -1,30 +1,52 @@
 """Benchmark of the paged-KV attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill|decode|reshape]
+                    [--only WORKLOAD] [--no-extras] [--no-cpu-baseline]
 
-Headline (default, --workload prefill): BASELINE config 2, a Llama-3-8B-shaped
-varlen causal prefill (4 sequences, lengths U{512..2048}, Hq 32, Hkv 8, D 128,
-bf16, 16-token pages).  One step = reshape_and_cache of every token into the
-paged cache + the tcgen05 prefill over the cache; metric = prefill TFLOP/s
-(algorithmic FLOPs 4*D*Hq*causal pairs).  Also reported in the same JSON line:
-the config-3 decode step (reshape of 64 new tokens + split-KV decode; HBM GB/s)
-and the config-4 reshape sweep point T=65536 scattered (HBM GB/s).
+Headline (every N, one process per GPU under torchrun): Llama-3-70B-shaped attention
+sharded by KV head, the configuration the metric "per GPU at 1/2/4/8 B200" names.
+Hq 64, Hkv 8, D 128, bf16, 16-token pages; rank r of N owns KV heads
+[r*8/N, (r+1)*8/N) and their Q heads, as its own tensors; no collective on the path.
+  * prefill step: reshape_and_cache of 2 x 8192 tokens into a contiguous cache + the
+    tcgen05 causal prefill over it.  value = aggregate prefill TFLOP/s of the job
+    (algorithmic FLOPs 4*D*Hq*causal pairs over all 64 heads / the slowest rank's
+    step time): strong scaling, the total work is fixed.
+  * decode step (same line, "decode"): 256 sequences with context U{1024..32768}
+    (seed 41), block tables from a random permutation of the page pool (seed 42),
+    reshape_and_cache of the 256 new tokens + split-KV decode; aggregate HBM GB/s.
+  * e2e: the prefill step through the public torch API with pinned host buffers,
+    every step's inputs copied host->device and its output device->host.
+  * verify: after timing, each rank's outputs on sampled rows / sequences are
+    gathered to rank 0 and checked against a plain torch fp32 attention on the GPU.
+Inputs are drawn per head from per-head seeds, so the job computes the same numbers
+at every N.
 
-Multi-GPU (torchrun, one rank per GPU): attention shards by sequence / KV head
-with no collective, so every rank runs its own config-2 batch (weak scaling);
-time = max over ranks of the device time of K steps.
+Extras at N=1 (same JSON line): the Llama-3-8B varlen prefill (4 sequences
+U{512..2048}, Hq 32, Hkv 8) with its own roofline, its e4m3-cache variant, the
+Llama-3-8B decode step (B 64, ctx U{512..8192}, 40k-page pool; unfused, fused, e4m3),
+the reshape_and_cache sweep (T in {1, 16, 256, 4096, 65536} x scattered / sequential
+x 0 / 10 % padding into a 65,536-page cache), the CPU-runnable fp16 pair (reshape
+T 256 + prefill L 256 on the GPU) and rms_norm with the residual add.
 
---impl reference times the reference's CPU implementation of the path (the
-oracle restatement of its goldens: numpy fp32 attention, C reshape loop) on the
-host cores, on bounded samples of the same workload.
+Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events on the
+launching stream; a step's time is the 10 %-trimmed mean of the K samples (the
+reference harness sorts its samples and drops 10 % at each end,
+test/src/suite/executor.cpp:270-276); the whole K-step region is bracketed by a
+barrier and a device synchronise; multi-GPU times are the max over ranks.  L2 is
+flushed (256 MB write) between timed prefill steps; decode and reshape inputs are
+larger than L2 unless stated otherwise per key.
+
+--impl reference times the reference's own CPU golden of the path on the host
+cores: flash_attn_varlen_func of test/zoo/teco/flash_attention/flash_attention.py
+(torch fp32, installed unmodified under baseline/_ref by oracle/install_ref.py), on
+a bounded sample of the same workload per step, plus the reshape_and_cache loop
+(this repository's C restatement; the reference's is a C++ harness method).
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -34,8 +56,9 @@ for _p in (ROOT, os.path.join(ROOT, "teco-ops_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-HQ, HKV, D, BS = 32, 8, 128, 16
+D, BS = 128, 16
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+TRIM = 0.10
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -51,24 +74,30 @@ def causal_pairs(q_lens, kv_lens):
     return tot
 
 
-def attn_flops(q_lens, kv_lens, hq=HQ, d=D):
+def attn_flops(q_lens, kv_lens, hq, d=D):
     return 4 * d * hq * causal_pairs(q_lens, kv_lens)
 
 
-def attn_bytes(q_lens, kv_lens, hq=HQ, hkv=HKV, d=D, bs=BS):
-    kv = sum(kv_lens) * hkv * d * 2 * 2
+def attn_bytes(q_lens, kv_lens, hq, hkv, d=D, bs=BS, elem=2):
+    kv = sum(kv_lens) * hkv * d * elem * 2
     qo = 2 * sum(q_lens) * hq * d * 2
     return kv + qo + 4 * sum(cdiv(s, bs) for s in kv_lens) + 8 * len(q_lens)
 
 
-def reshape_bytes(n_valid, n_tokens, hkv=HKV, d=D):
+def reshape_bytes(n_valid, n_tokens, hkv, d=D):
     return 8 * n_tokens + 4 * n_valid * hkv * d * 2
 
 
+def trimmed_mean(xs, frac=TRIM):
+    s = sorted(xs)
+    k = int(len(s) * frac)
+    s = s[k:len(s) - k] if len(s) - 2 * k > 0 else s
+    return sum(s) / len(s)
+
+
 def load_peaks():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        with open(p) as f:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             j = json.load(f)
         return {k: float(j[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, \
             "measured"
@@ -83,12 +112,6 @@ def load_traffic():
             return json.load(f)
     except Exception:
         return {}
-
-
-def config2_lens(seed=10):
-    import torch
-    g = torch.Generator().manual_seed(seed)
-    return torch.randint(512, 2049, (4,), generator=g).tolist()
 
 
 class ClockSampler:
@@ -147,237 +170,10 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ----------------------------------------------------------------------------- our arm
-class Workloads:
-    """Device-resident inputs of the three benchmarked configurations."""
-
-    def __init__(self, rank: int):
-        import torch
-        from tecoops import capi
-        self.torch = torch
-        self.capi = capi
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.dev = dev
-        g = torch.Generator(device=dev).manual_seed(1000 + rank)
-        bf = torch.bfloat16
-        # ---- config 2: varlen prefill
-        self.lens = config2_lens()
-        tot = sum(self.lens)
-        self.tot = tot
-        self.q = torch.randn(tot, HQ, D, device=dev, dtype=bf, generator=g)
-        self.k = torch.randn(tot, HKV, D, device=dev, dtype=bf, generator=g)
-        self.v = torch.randn(tot, HKV, D, device=dev, dtype=bf, generator=g)
-        pages = [cdiv(l, BS) for l in self.lens]
-        self.nb = sum(pages)
-        bt = torch.zeros(len(self.lens), max(pages), dtype=torch.int32)
-        slots, p0 = [], 0
-        for b, l in enumerate(self.lens):
-            bt[b, :pages[b]] = torch.arange(p0, p0 + pages[b], dtype=torch.int32)
-            slots.append(torch.arange(l) + p0 * BS)
-            p0 += pages[b]
-        self.bt = bt.to(dev)
-        self.slot = torch.cat(slots).to(dev)
-        self.kc = torch.zeros(self.nb, HKV, BS, D, device=dev, dtype=bf)
-        self.vc = torch.zeros_like(self.kc)
-        self.qlens = torch.tensor(self.lens, dtype=torch.int32, device=dev)
-        self.out = torch.empty_like(self.q)
-        self.flops = attn_flops(self.lens, self.lens)
-        self.h = capi.Handle()
-        self.d_bt = capi.Desc(capi.DATA_INT32, self.bt.shape)
-        self.d_q = capi.Desc(capi.DATA_BFLOAT16, self.q.shape)
-        self.d_c = capi.Desc(capi.DATA_BFLOAT16, self.kc.shape)
-        self.d_o = capi.Desc(capi.DATA_BFLOAT16, self.out.shape)
-        self.max_q = max(self.lens)
-        self.reshape_bytes2 = reshape_bytes(tot, tot)
-        # L2 flush buffer (> 126 MB L2)
-        self.flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
-
-    def set_stream(self):
-        self.h.set_stream(self.torch.cuda.current_stream().cuda_stream)
-
-    def flush(self):
-        self.flush_buf.zero_()
-
-    def reshape2(self):
-        st = self.capi.reshape_and_cache(self.h, self.k.data_ptr(), self.v.data_ptr(),
-                                         self.slot.data_ptr(), self.kc.data_ptr(),
-                                         self.vc.data_ptr(), self.tot, HKV, D, self.nb, BS)
-        self.capi.check(st, "reshape_and_cache")
-
-    def prefill2(self):
-        st = self.capi.flash_attention(self.h, self.max_q, self.max_q, self.nb,
-                                       self.qlens.data_ptr(), self.qlens.data_ptr(), self.d_bt,
-                                       self.bt.data_ptr(), self.d_q, self.q.data_ptr(), self.d_c,
-                                       self.kc.data_ptr(), self.d_c, self.vc.data_ptr(), self.d_o,
-                                       self.out.data_ptr())
-        self.capi.check(st, "flash_attention")
-
-    # ---- config 3: decode
-    def setup_decode(self, rank: int):
-        torch = self.torch
-        B, pool = 64, 40000
-        g = torch.Generator().manual_seed(20)
-        ctx = torch.randint(512, 8193, (B,), generator=g)
-        perm = torch.randperm(pool, generator=torch.Generator().manual_seed(21)).to(torch.int32)
-        pages = cdiv(ctx + 1, BS).tolist()
-        bt = torch.zeros(B, max(pages), dtype=torch.int32)
-        p0 = 0
-        for b in range(B):
-            bt[b, :pages[b]] = perm[p0:p0 + pages[b]]
-            p0 += pages[b]
-        gd = torch.Generator(device=self.dev).manual_seed(2200 + rank)
-        bf = torch.bfloat16
-        self.d_kc = torch.randn(pool, HKV, BS, D, device=self.dev, dtype=bf, generator=gd)
-        self.d_vc = torch.randn(pool, HKV, BS, D, device=self.dev, dtype=bf, generator=gd)
-        self.d_q3 = torch.randn(B, HQ, D, device=self.dev, dtype=bf, generator=gd)
-        self.d_knew = torch.randn(B, HKV, D, device=self.dev, dtype=bf, generator=gd)
-        self.d_vnew = torch.randn(B, HKV, D, device=self.dev, dtype=bf, generator=gd)
-        # new token of sequence b goes to position ctx[b] (its next position)
-        slot = [int(bt[b, int(ctx[b]) // BS]) * BS + int(ctx[b]) % BS for b in range(B)]
-        self.d_slot = torch.tensor(slot, dtype=torch.int64, device=self.dev)
-        self.d_ctx = (ctx + 1).to(torch.int32).to(self.dev)
-        self.d_ones = torch.ones(B, dtype=torch.int32, device=self.dev)
-        self.d_bt3 = bt.to(self.dev)
-        self.d_out3 = torch.empty_like(self.d_q3)
-        self.d_desc = (self.capi.Desc(self.capi.DATA_INT32, bt.shape),
-                       self.capi.Desc(self.capi.DATA_BFLOAT16, self.d_q3.shape),
-                       self.capi.Desc(self.capi.DATA_BFLOAT16, self.d_kc.shape))
-        self.d_B, self.d_pool = B, pool
-        self.d_maxk = int(ctx.max()) + 1
-        kv = (ctx + 1).tolist()
-        self.decode_bytes = attn_bytes([1] * B, kv)
-        self.decode_reshape_bytes = reshape_bytes(B, B)
-
-    def decode_step(self):
-        st = self.capi.reshape_and_cache(self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(),
-                                         self.d_slot.data_ptr(), self.d_kc.data_ptr(),
-                                         self.d_vc.data_ptr(), self.d_B, HKV, D, self.d_pool, BS)
-        self.capi.check(st, "reshape_and_cache")
-
-    def decode_attn(self):
-        bt_d, q_d, c_d = self.d_desc
-        st = self.capi.flash_attention(self.h, 1, self.d_maxk, self.d_pool, self.d_ones.data_ptr(),
-                                       self.d_ctx.data_ptr(), bt_d, self.d_bt3.data_ptr(), q_d,
-                                       self.d_q3.data_ptr(), c_d, self.d_kc.data_ptr(), c_d,
-                                       self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr())
-        self.capi.check(st, "flash_attention")
-
-    def decode_fused(self):
-        """The same step through tecoopsReshapeAndCacheFlashAttentionDecode (one launch
-        for the scatter and the split-KV pass, plus the split merge)."""
-        bt_d, q_d, c_d = self.d_desc
-        st = self.capi.reshape_and_cache_flash_attention_decode(
-            self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(), self.d_slot.data_ptr(),
-            self.d_maxk, self.d_ones.data_ptr(), self.d_ctx.data_ptr(), bt_d,
-            self.d_bt3.data_ptr(), q_d, self.d_q3.data_ptr(), c_d, self.d_kc.data_ptr(), c_d,
-            self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr())
-        self.capi.check(st, "reshape_and_cache_flash_attention_decode")
-
-    # ---- config 2 on an e4m3 cache (extension): reshape_ex quantises, prefill_ex reads it
-    def setup_prefill_fp8(self):
-        capi, torch = self.capi, self.torch
-        self.p8_ks = self.p8_vs = 1.0 / 64
-        self.p8_kc = torch.zeros(self.kc.shape, dtype=torch.uint8, device=self.dev)
-        self.p8_vc = torch.zeros_like(self.p8_kc)
-        self.p8_desc = capi.Desc(capi.DATA_FLOAT8_E4M3, self.p8_kc.shape)
-
-    def reshape2_fp8(self):
-        capi = self.capi
-        st = capi.reshape_and_cache_ex(self.h, self.k.data_ptr(), self.v.data_ptr(),
-                                       self.slot.data_ptr(), self.p8_kc.data_ptr(),
-                                       self.p8_vc.data_ptr(), self.tot, HKV, D, self.nb, BS,
-                                       capi.DATA_BFLOAT16, cache_dtype=capi.DATA_FLOAT8_E4M3,
-                                       k_scale=self.p8_ks, v_scale=self.p8_vs)
-        capi.check(st, "reshape_and_cache_ex fp8")
-
-    def prefill2_fp8(self):
-        capi = self.capi
-        st = capi.flash_attention_ex(self.h, self.max_q, self.max_q, self.nb,
-                                     self.qlens.data_ptr(), self.qlens.data_ptr(), self.d_bt,
-                                     self.bt.data_ptr(), self.d_q, self.q.data_ptr(),
-                                     self.p8_desc, self.p8_kc.data_ptr(), self.p8_desc,
-                                     self.p8_vc.data_ptr(), self.d_o, self.out.data_ptr(),
-                                     k_scale=self.p8_ks, v_scale=self.p8_vs)
-        capi.check(st, "flash_attention_ex fp8")
-
-    # ---- rms_norm (the op before the QKV projection), residual form
-    def setup_rms(self):
-        torch = self.torch
-        self.n_T, hidden = 16 * self.tot, 4096
-        g = torch.Generator(device=self.dev).manual_seed(4000)
-        bf = torch.bfloat16
-        self.n_x = torch.randn(self.n_T, hidden, device=self.dev, dtype=bf, generator=g)
-        self.n_r = torch.randn(self.n_T, hidden, device=self.dev, dtype=bf, generator=g)
-        self.n_w = torch.randn(hidden, device=self.dev, dtype=bf, generator=g)
-        self.n_y = torch.empty_like(self.n_x)
-        self.n_ro = torch.empty_like(self.n_x)
-        self.n_bytes = self.n_T * hidden * 2 * 4 + hidden * 2   # x, r in; y, r_out out; w
-
-    def rms_step(self):
-        capi = self.capi
-        st = capi.rms_norm(self.h, self.n_x.data_ptr(), self.n_w.data_ptr(), self.n_r.data_ptr(),
-                           self.n_y.data_ptr(), self.n_ro.data_ptr(), self.n_T, 4096, 1e-6,
-                           dtype=capi.DATA_BFLOAT16)
-        capi.check(st, "rms_norm")
-
-    # ---- config 3 on an e4m3 cache (extension): same shapes, half the cache bytes
-    def setup_decode_fp8(self):
-        torch, capi = self.torch, self.capi
-        self.f_ks, self.f_vs = 1.0 / 64, 1.0 / 64
-        self.f_kc = (self.d_kc.float() / self.f_ks).to(torch.float8_e4m3fn).view(torch.uint8)
-        self.f_vc = (self.d_vc.float() / self.f_vs).to(torch.float8_e4m3fn).view(torch.uint8)
-        self.f_desc = capi.Desc(capi.DATA_FLOAT8_E4M3, self.f_kc.shape)
-        B = self.d_B
-        kv = self.d_ctx.cpu().tolist()
-        self.f_bytes = (sum(kv) * HKV * D * 1 * 2 + 2 * B * HQ * D * 2
-                        + 4 * sum(cdiv(k, BS) for k in kv))
-        self.f_reshape_bytes = 8 * B + 2 * B * HKV * D * 2 + 2 * B * HKV * D * 1
-
-    def decode_fp8_step(self):
-        capi = self.capi
-        st = capi.reshape_and_cache_ex(self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(),
-                                       self.d_slot.data_ptr(), self.f_kc.data_ptr(),
-                                       self.f_vc.data_ptr(), self.d_B, HKV, D, self.d_pool, BS,
-                                       capi.DATA_BFLOAT16, cache_dtype=capi.DATA_FLOAT8_E4M3,
-                                       k_scale=self.f_ks, v_scale=self.f_vs)
-        capi.check(st, "reshape_and_cache_ex fp8")
-
-    def decode_fp8_attn(self):
-        capi = self.capi
-        bt_d, q_d, _ = self.d_desc
-        st = capi.flash_attention_ex(self.h, 1, self.d_maxk, self.d_pool, self.d_ones.data_ptr(),
-                                     self.d_ctx.data_ptr(), bt_d, self.d_bt3.data_ptr(), q_d,
-                                     self.d_q3.data_ptr(), self.f_desc, self.f_kc.data_ptr(),
-                                     self.f_desc, self.f_vc.data_ptr(), q_d,
-                                     self.d_out3.data_ptr(), k_scale=self.f_ks,
-                                     v_scale=self.f_vs)
-        capi.check(st, "flash_attention_ex fp8")
-
-    # ---- config 4: reshape sweep point (T = 65536, scattered, no padding)
-    def setup_reshape(self, rank: int):
-        torch = self.torch
-        T, NB = 65536, 65536
-        g = torch.Generator(device=self.dev).manual_seed(3000 + rank)
-        bf = torch.bfloat16
-        self.r_k = torch.randn(T, HKV, D, device=self.dev, dtype=bf, generator=g)
-        self.r_v = torch.randn(T, HKV, D, device=self.dev, dtype=bf, generator=g)
-        self.r_slot = torch.randperm(NB * BS, device=self.dev, generator=g)[:T].contiguous()
-        self.r_kc = torch.zeros(NB, HKV, BS, D, device=self.dev, dtype=bf)
-        self.r_vc = torch.zeros_like(self.r_kc)
-        self.r_T, self.r_NB = T, NB
-        self.r_bytes = reshape_bytes(T, T)
-
-    def reshape4(self):
-        st = self.capi.reshape_and_cache(self.h, self.r_k.data_ptr(), self.r_v.data_ptr(),
-                                         self.r_slot.data_ptr(), self.r_kc.data_ptr(),
-                                         self.r_vc.data_ptr(), self.r_T, HKV, D, self.r_NB, BS)
-        self.capi.check(st, "reshape_and_cache")
-
-
 def timed_loop(torch, steps, warmup, phases, flush=None):
-    """Run `warmup` then `steps` iterations of the callables in `phases`, each
-    bracketed by CUDA events on the current stream; `flush` runs untimed between
-    iterations.  Returns per-phase lists of ms."""
+    """`warmup` untimed iterations, then `steps` iterations of the callables in
+    `phases`, each phase bracketed by CUDA events on the current stream; `flush`
+    runs between iterations, outside the events.  Returns per-phase lists of ms."""
     for _ in range(warmup):
         for f in phases:
             f()
@@ -394,218 +190,121 @@ def timed_loop(torch, steps, warmup, phases, flush=None):
         if flush:
             flush()
     torch.cuda.synchronize()
-    out = [[ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(steps)]
-           for i in range(len(phases))]
+    return [[ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(steps)]
+            for i in range(len(phases))]
+
+
+def step_ms(times):
+    """Per-step time of a phase list: 10 %-trimmed mean of the summed phases."""
+    return trimmed_mean([sum(x) for x in zip(*times)])
+
+
+class Dist:
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max(self, x):
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([float(x)], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def per_head_randn(torch, lead_shape, heads, seed0, dev, dtype):
+    """[*lead_shape[:1], len(heads), *lead_shape[1:]] with head h drawn from seed0 + h
+    (the global head index), so a shard holds the same values at every N."""
+    out = torch.empty(lead_shape[0], len(heads), *lead_shape[1:], device=dev, dtype=dtype)
+    g = torch.Generator(device=dev)
+    for i, h in enumerate(heads):
+        g.manual_seed(seed0 + h)
+        out[:, i] = torch.randn(*lead_shape, device=dev, dtype=dtype, generator=g)
     return out
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    W = Workloads(rank)
-    W.set_stream()
-    peaks, peak_src = load_peaks()
-    if args.only:
-        run_only(W, args, torch, rank)
-        return
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---------------- headline: config 2 prefill step
-    clocks = ClockSampler(local)
-    barrier()
-    clocks.start()
-    times = timed_loop(torch, args.steps, args.warmup, [W.reshape2, W.prefill2], flush=W.flush)
-    barrier()
-    t_reshape, t_prefill = times
-    step_ms = [a + b for a, b in zip(t_reshape, t_prefill)]
-    total_ms = max_over_ranks(sum(step_ms))
-    value = world * args.steps * W.flops / (total_ms * 1e-3) / 1e12
-    avg_prefill_ms = sum(t_prefill) / len(t_prefill)
-    achieved = W.flops / (avg_prefill_ms * 1e-3) / 1e12
-    traffic = load_traffic().get("fa_prefill_tcgen05_sm100/config2")
-
-    # ---------------- config 2 on an e4m3 cache (dequantised compact copy + tcgen05)
-    W.setup_prefill_fp8()
-    fr8, fp8t = timed_loop(torch, args.steps, args.warmup, [W.reshape2_fp8, W.prefill2_fp8],
-                           flush=W.flush)
-    p8_ms = max_over_ranks(sum(a + b for a, b in zip(fr8, fp8t)))
-    prefill_fp8 = {"api": "tecoopsReshapeAndCacheEx + tecoopsFlashAttentionEx, e4m3 cache",
-                   "value": world * args.steps * W.flops / (p8_ms * 1e-3) / 1e12,
-                   "unit": "TFLOP/s", "ms_per_step": p8_ms / args.steps,
-                   "prefill_us": sum(fp8t) / len(fp8t) * 1e3}
-
-    # ---------------- e2e: public torch API, host buffers, H2D + D2H in the timed region
-    e2e = run_e2e(W, args, torch, world, max_over_ranks, barrier)
-
-    # ---------------- secondary: config 3 decode step and config 4 reshape point
-    W.setup_decode(rank)
-    barrier()
-    tr, ta = timed_loop(torch, args.steps, args.warmup, [W.decode_step, W.decode_attn])
-    dec_ms = max_over_ranks(sum(a + b for a, b in zip(tr, ta)))
-    dec_attn_avg = sum(ta) / len(ta)
-    dec_bytes_step = W.decode_bytes + W.decode_reshape_bytes
-    (tf,) = timed_loop(torch, args.steps, args.warmup, [W.decode_fused])
-    dec_fused_ms = max_over_ranks(sum(tf))
-    W.setup_decode_fp8()
-    fr, fa = timed_loop(torch, args.steps, args.warmup, [W.decode_fp8_step, W.decode_fp8_attn])
-    f_ms = max_over_ranks(sum(a + b for a, b in zip(fr, fa)))
-    f_attn_avg = sum(fa) / len(fa)
-    decode = {
-        "workload": "config 3: B=64 paged decode, ctx U{512..8192}+1, 40k-page pool, bs 16, bf16",
-        "metric": "decode HBM GB/s", "unit": "GB/s",
-        "value": world * args.steps * dec_bytes_step / (dec_ms * 1e-3) / 1e9,
-        "ms_per_step": dec_ms / args.steps,
-        "attn_kernel_us": dec_attn_avg * 1e3,
-        "attn_gbs": W.decode_bytes / (dec_attn_avg * 1e-3) / 1e9,
-        "attn_frac_of_measured_hbm": W.decode_bytes / (dec_attn_avg * 1e-3) / 1e9 / peaks["hbm_gbs"],
-        "l2": "inputs (1.1 GB of K/V) larger than L2",
-        "fused": {"api": "tecoopsReshapeAndCacheFlashAttentionDecode (scatter + attention in "
-                         "one launch, same bytes)",
-                  "ms_per_step": dec_fused_ms / args.steps,
-                  "value": world * args.steps * dec_bytes_step / (dec_fused_ms * 1e-3) / 1e9},
-        "fp8_cache": {"api": "tecoopsReshapeAndCacheEx + tecoopsFlashAttentionEx, e4m3 cache "
-                             "(k/v scale 1/64), same shapes",
-                      "ms_per_step": f_ms / args.steps,
-                      "value": world * args.steps * (W.f_bytes + W.f_reshape_bytes)
-                      / (f_ms * 1e-3) / 1e9,
-                      "attn_kernel_us": f_attn_avg * 1e3,
-                      "attn_gbs": W.f_bytes / (f_attn_avg * 1e-3) / 1e9,
-                      "attn_frac_of_measured_hbm": W.f_bytes / (f_attn_avg * 1e-3) / 1e9
-                      / peaks["hbm_gbs"],
-                      "speedup_vs_bf16_step": (dec_ms / args.steps) / (f_ms / args.steps)},
-    }
-    del W.d_kc, W.d_vc, W.f_kc, W.f_vc
-    torch.cuda.empty_cache()
-    W.setup_reshape(rank)
-    barrier()
-    (t4,) = timed_loop(torch, args.steps, args.warmup, [W.reshape4])
-    r_ms = max_over_ranks(sum(t4))
-    del W.r_kc, W.r_vc
-    W.setup_rms()
-    (tn,) = timed_loop(torch, args.steps, args.warmup, [W.rms_step])
-    n_ms = max_over_ranks(sum(tn))
-    clk = clocks.stop()   # sampled across every timed region above
-    reshape = {
-        "workload": "config 4: T=65536 scattered slots, 0% padding, 65536-page cache, bf16",
-        "metric": "reshape_and_cache HBM GB/s", "unit": "GB/s",
-        "value": world * args.steps * W.r_bytes / (r_ms * 1e-3) / 1e9,
-        "kernel_us": r_ms / args.steps * 1e3,
-        "frac_of_measured_hbm": W.r_bytes / (r_ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"],
-        "l2": "inputs (537 MB) larger than L2",
-    }
-    rms = {
-        "workload": f"rms_norm with residual add, {W.n_T} tokens x hidden 4096 (Llama-3-8B "
-                    "layer input of config 2, 16 steps' worth), bf16",
-        "metric": "rms_norm HBM GB/s", "unit": "GB/s",
-        "value": world * args.steps * W.n_bytes / (n_ms * 1e-3) / 1e9,
-        "kernel_us": n_ms / args.steps * 1e3,
-        "frac_of_measured_hbm": W.n_bytes / (n_ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"],
-        "l2": f"inputs ({W.n_bytes / 1e6:.0f} MB) larger than L2",
-    }
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_prefill(W.lens, budget_s=args.cpu_budget)
-
-    if rank == 0:
-        line = {
-            "metric": "prefill TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) Q/K/V, Llama-3-8B head shapes)",
-            "config": {"workload": "config 2: varlen causal prefill, 4 seqs L~U{512..2048} "
-                                   f"({'+'.join(map(str, W.lens))} tokens), Hq 32, Hkv 8, D 128, "
-                                   "bs 16, reshape_and_cache of all tokens + prefill",
-                       "seq_lens": W.lens, "parallelism": f"{world} independent shards (no collective)",
-                       "l2": "flushed between timed steps (256 MB write)"},
-            "gpu_launches": 2 * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "fa_prefill_tcgen05_sm100",
-                         "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": achieved / peaks["bf16_tflops"],
-                         "peak_source": f"{peak_src} bf16_tflops (burst)",
-                         "traffic": traffic, "flops_per_launch": W.flops,
-                         "kernel_us": avg_prefill_ms * 1e3},
-            "reshape_us_per_step": sum(t_reshape) / len(t_reshape) * 1e3,
-            "e2e": e2e,
-            "clocks": clk,
-            "decode": decode,
-            "reshape": reshape,
-            "rms_norm": rms,
-            "prefill_fp8_cache": prefill_fp8,
-        }
-        if cpu is not None:
-            line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+def torch_attention_rows(torch, q_rows, pos, k, v, group, scale):
+    """Plain torch fp32 attention of query rows at positions `pos` (causal: keys
+    j <= pos) over keys k / values v [S, Hkv, D]; q_rows [R, Hq, D] -> [R, Hq, D]."""
+    qf = q_rows.float().permute(1, 0, 2)                                  # [Hq, R, D]
+    kf = k.float().permute(1, 2, 0).repeat_interleave(group, 0)           # [Hq, D, S]
+    vf = v.float().permute(1, 0, 2).repeat_interleave(group, 0)           # [Hq, S, D]
+    s = torch.matmul(qf, kf) * scale
+    j = torch.arange(k.shape[0], device=k.device)
+    s = s.masked_fill(j[None, None, :] > pos[None, :, None], float("-inf"))
+    return torch.matmul(torch.softmax(s, -1), vf).permute(1, 0, 2)
 
 
+def err_stats(torch, got, ref):
+    d = (got.float() - ref.float()).abs()
+    mx, mean = float(d.max()), float(d.mean())
+    return {"max_abs": mx, "mean_abs": mean, "ok": bool(mx <= 2e-2 and mean <= 2e-3)}
+
+
+# ----------------------------------------------------------------------------- headline
 class Llama70B:
-    """BASELINE config 5, Llama-3-70B-shaped attention sharded by KV head: Hq 64, Hkv 8,
-    D 128, bf16, bs 16.  Prefill: 2 sequences of 8192 tokens (causal), K/V written by
-    reshape_and_cache into a contiguous cache.  Decode: 256 sequences with context
-    U{1024..32768} (seed 41), block tables from a random permutation of the page pool
-    (seed 42), plus reshape of the 256 new tokens.  Rank r of G owns KV heads
-    [r*8/G, (r+1)*8/G) (strong scaling, no collective)."""
+    """Llama-3-70B-shaped attention sharded by KV head (Hq 64, Hkv 8, D 128, bf16, bs 16)."""
 
-    HQ, HKV = 64, 8
+    HQ, HKV, L, NSEQ, B_DEC = 64, 8, 8192, 2, 256
+    SEED_Q, SEED_K, SEED_V = 50000, 51000, 52000
+    SEED_DK, SEED_DV, SEED_DQ, SEED_NK, SEED_NV = 53000, 54000, 55000, 56000, 57000
 
-    def __init__(self, rank, world, with_decode=True):
+    def __init__(self, dd: Dist, with_decode=True):
         import torch
         from tecoops import capi, sharding
-        self.torch, self.capi = torch, capi
+        self.torch, self.capi, self.dd = torch, capi, dd
         dev = torch.device("cuda", torch.cuda.current_device())
-        s = sharding.head_shard(self.HQ, self.HKV, world, rank)
+        self.dev = dev
+        self.shard = s = sharding.head_shard(self.HQ, self.HKV, dd.world, dd.rank)
         self.hq, self.hkv = s.q_heads, s.kv_heads
+        self.qh = list(range(s.q_begin, s.q_end))
+        self.kh = list(range(s.kv_begin, s.kv_end))
         bf = torch.bfloat16
-        g = torch.Generator(device=dev).manual_seed(40 + rank)
-        # ---- prefill
-        self.lens = [8192, 8192]
+        self.lens = [self.L] * self.NSEQ
         tot = sum(self.lens)
-        self.q = torch.randn(tot, self.hq, D, device=dev, dtype=bf, generator=g)
-        self.k = torch.randn(tot, self.hkv, D, device=dev, dtype=bf, generator=g)
-        self.v = torch.randn(tot, self.hkv, D, device=dev, dtype=bf, generator=g)
-        pages = [cdiv(l, BS) for l in self.lens]
+        self.tot = tot
+        self.q = per_head_randn(torch, (tot, D), self.qh, self.SEED_Q, dev, bf)
+        self.k = per_head_randn(torch, (tot, D), self.kh, self.SEED_K, dev, bf)
+        self.v = per_head_randn(torch, (tot, D), self.kh, self.SEED_V, dev, bf)
+        pages = [cdiv(n, BS) for n in self.lens]
         self.nb = sum(pages)
-        bt = torch.zeros(2, max(pages), dtype=torch.int32)
-        bt[0, :pages[0]] = torch.arange(pages[0], dtype=torch.int32)
-        bt[1, :pages[1]] = torch.arange(pages[0], pages[0] + pages[1], dtype=torch.int32)
+        bt = torch.arange(self.nb, dtype=torch.int32).view(self.NSEQ, -1)
         self.bt = bt.to(dev)
         self.slot = torch.arange(tot, device=dev)
         self.kc = torch.zeros(self.nb, self.hkv, BS, D, device=dev, dtype=bf)
         self.vc = torch.zeros_like(self.kc)
         self.qlens = torch.tensor(self.lens, dtype=torch.int32, device=dev)
         self.out = torch.empty_like(self.q)
-        self.flops = attn_flops(self.lens, self.lens, hq=self.hq)
+        self.flops_total = attn_flops(self.lens, self.lens, hq=self.HQ)
+        self.flops_local = attn_flops(self.lens, self.lens, hq=self.hq)
         self.h = capi.Handle(torch.cuda.current_stream().cuda_stream)
-        self.d = (capi.Desc(capi.DATA_INT32, self.bt.shape), capi.Desc(capi.DATA_BFLOAT16, self.q.shape),
+        self.d = (capi.Desc(capi.DATA_INT32, self.bt.shape),
+                  capi.Desc(capi.DATA_BFLOAT16, self.q.shape),
                   capi.Desc(capi.DATA_BFLOAT16, self.kc.shape))
         self.flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
         if with_decode:
-            self._setup_decode(dev, rank)
+            self._setup_decode()
 
-    def _setup_decode(self, dev, rank):
-        torch, capi = self.torch, self.capi
-        B = 256
+    def _setup_decode(self):
+        torch, capi, dev = self.torch, self.capi, self.dev
+        B = self.B_DEC
         ctx = torch.randint(1024, 32769, (B,), generator=torch.Generator().manual_seed(41))
         pages = cdiv(ctx + 1, BS).tolist()
         pool = sum(pages) + 1024
@@ -615,146 +314,140 @@ class Llama70B:
         for b in range(B):
             bt[b, :pages[b]] = perm[p0:p0 + pages[b]]
             p0 += pages[b]
-        g = torch.Generator(device=dev).manual_seed(4100 + rank)
         bf = torch.bfloat16
-        self.dkc = torch.randn(pool, self.hkv, BS, D, device=dev, dtype=bf, generator=g)
-        self.dvc = torch.randn(pool, self.hkv, BS, D, device=dev, dtype=bf, generator=g)
-        self.dq = torch.randn(B, self.hq, D, device=dev, dtype=bf, generator=g)
-        self.dknew = torch.randn(B, self.hkv, D, device=dev, dtype=bf, generator=g)
-        self.dvnew = torch.randn(B, self.hkv, D, device=dev, dtype=bf, generator=g)
+        self.dkc = per_head_randn(torch, (pool, BS, D), self.kh, self.SEED_DK, dev, bf)
+        self.dvc = per_head_randn(torch, (pool, BS, D), self.kh, self.SEED_DV, dev, bf)
+        self.dq = per_head_randn(torch, (B, D), self.qh, self.SEED_DQ, dev, bf)
+        self.dknew = per_head_randn(torch, (B, D), self.kh, self.SEED_NK, dev, bf)
+        self.dvnew = per_head_randn(torch, (B, D), self.kh, self.SEED_NV, dev, bf)
         slot = [int(bt[b, int(ctx[b]) // BS]) * BS + int(ctx[b]) % BS for b in range(B)]
         self.dslot = torch.tensor(slot, dtype=torch.int64, device=dev)
+        self.dctx_h = ctx
+        self.dbt_h = bt
         self.dctx = (ctx + 1).to(torch.int32).to(dev)
         self.dones = torch.ones(B, dtype=torch.int32, device=dev)
         self.dbt = bt.to(dev)
         self.dout = torch.empty_like(self.dq)
-        self.dd = (capi.Desc(capi.DATA_INT32, bt.shape), capi.Desc(capi.DATA_BFLOAT16, self.dq.shape),
-                   capi.Desc(capi.DATA_BFLOAT16, self.dkc.shape))
+        self.dd_ = (capi.Desc(capi.DATA_INT32, bt.shape),
+                    capi.Desc(capi.DATA_BFLOAT16, self.dq.shape),
+                    capi.Desc(capi.DATA_BFLOAT16, self.dkc.shape))
         self.dB, self.dpool, self.dmaxk = B, pool, int(ctx.max()) + 1
-        self.dbytes = attn_bytes([1] * B, (ctx + 1).tolist(), hq=self.hq, hkv=self.hkv) + \
+        kv = (ctx + 1).tolist()
+        self.dbytes_total = attn_bytes([1] * B, kv, hq=self.HQ, hkv=self.HKV) + \
+            reshape_bytes(B, B, hkv=self.HKV)
+        self.dbytes_local = attn_bytes([1] * B, kv, hq=self.hq, hkv=self.hkv) + \
             reshape_bytes(B, B, hkv=self.hkv)
+        self.d_attn_bytes_local = attn_bytes([1] * B, kv, hq=self.hq, hkv=self.hkv)
+
+    def flush(self):
+        self.flush_buf.zero_()
 
     def reshape(self):
-        tot = sum(self.lens)
         self.capi.check(self.capi.reshape_and_cache(
             self.h, self.k.data_ptr(), self.v.data_ptr(), self.slot.data_ptr(), self.kc.data_ptr(),
-            self.vc.data_ptr(), tot, self.hkv, D, self.nb, BS), "reshape")
+            self.vc.data_ptr(), self.tot, self.hkv, D, self.nb, BS), "reshape_and_cache")
 
     def prefill(self):
         b, q, c = self.d
         self.capi.check(self.capi.flash_attention(
-            self.h, 8192, 8192, self.nb, self.qlens.data_ptr(), self.qlens.data_ptr(), b,
+            self.h, self.L, self.L, self.nb, self.qlens.data_ptr(), self.qlens.data_ptr(), b,
             self.bt.data_ptr(), q, self.q.data_ptr(), c, self.kc.data_ptr(), c, self.vc.data_ptr(),
-            q, self.out.data_ptr()), "prefill")
+            q, self.out.data_ptr()), "flash_attention prefill")
 
-    def decode(self):
+    def decode_reshape(self):
         self.capi.check(self.capi.reshape_and_cache(
             self.h, self.dknew.data_ptr(), self.dvnew.data_ptr(), self.dslot.data_ptr(),
-            self.dkc.data_ptr(), self.dvc.data_ptr(), self.dB, self.hkv, D, self.dpool, BS), "reshape")
-        b, q, c = self.dd
+            self.dkc.data_ptr(), self.dvc.data_ptr(), self.dB, self.hkv, D, self.dpool, BS),
+            "reshape_and_cache decode")
+
+    def decode(self):
+        b, q, c = self.dd_
         self.capi.check(self.capi.flash_attention(
             self.h, 1, self.dmaxk, self.dpool, self.dones.data_ptr(), self.dctx.data_ptr(), b,
             self.dbt.data_ptr(), q, self.dq.data_ptr(), c, self.dkc.data_ptr(), c,
-            self.dvc.data_ptr(), q, self.dout.data_ptr()), "decode")
+            self.dvc.data_ptr(), q, self.dout.data_ptr()), "flash_attention decode")
 
-
-def run_70b(args):
-    import torch
-    import torch.distributed as dist
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    W = Llama70B(rank, world)
-    peaks, peak_src = load_peaks()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x):
-        if world == 1:
+    # ---- verification (outside every timed region)
+    def _gather_heads(self, x):
+        """[R, Hq/N, D] on every rank -> [R, Hq, D] on every rank (head order)."""
+        torch, dd = self.torch, self.dd
+        if dd.world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        parts = [torch.empty_like(x) for _ in range(dd.world)]
+        dd.dist.all_gather(parts, x.contiguous())
+        return torch.cat(parts, dim=1)
 
-    clocks = ClockSampler(local)
-    barrier()
-    clocks.start()
-    tr, tp = timed_loop(torch, args.steps, args.warmup, [W.reshape, W.prefill],
-                        flush=lambda: W.flush_buf.zero_())
-    barrier()
-    ms = max_over_ranks(sum(a + b for a, b in zip(tr, tp)))
-    total_flops = attn_flops(W.lens, W.lens, hq=Llama70B.HQ)
-    (td,) = timed_loop(torch, args.steps, args.warmup, [W.decode])
-    barrier()
-    dms = max_over_ranks(sum(td))
-    clk = clocks.stop()
-    kern_ms = sum(tp) / len(tp)
-    if rank == 0:
-        print(json.dumps({
-            "metric": "prefill TFLOP/s", "value": args.steps * total_flops / (ms * 1e-3) / 1e12,
-            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
-            "config": {"workload": "config 5: Llama-3-70B heads (Hq 64, Hkv 8, D 128), prefill "
-                                   "2 x 8192 causal (reshape + prefill per step), KV-head sharded",
-                       "parallelism": f"KV heads split over {world} GPUs, no collective",
-                       "l2": "flushed between timed prefill steps"},
-            "gpu_launches": 2 * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "fa_prefill_tcgen05_sm100",
-                         "achieved": W.flops / (kern_ms * 1e-3) / 1e12,
-                         "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                         "frac": W.flops / (kern_ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
-                         "peak_source": f"{peak_src} bf16_tflops_sustained (long kernel)",
-                         "traffic": None},
-            "decode": {"workload": "config 5 decode: B 256, ctx U{1024..32768}, KV-head sharded",
-                       "metric": "decode HBM GB/s", "unit": "GB/s",
-                       "value": world * args.steps * W.dbytes / (dms * 1e-3) / 1e9,
-                       "ms_per_step": dms / args.steps,
-                       "per_gpu_frac_of_measured_hbm":
-                           args.steps * W.dbytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
-            "clocks": clk}), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def run_only(W, args, torch, rank):
-    """One workload's timed loop (profiler captures run this)."""
-    if args.only == "prefill":
-        ph, fl = [W.reshape2, W.prefill2], W.flush
-    elif args.only == "decode":
-        W.setup_decode(rank)
-        ph, fl = [W.decode_step, W.decode_attn], None
-    elif args.only == "rms_norm":
-        W.setup_rms()
-        ph, fl = [W.rms_step], None
-    elif args.only == "decode_fp8":
-        W.setup_decode(rank)
-        W.setup_decode_fp8()
-        ph, fl = [W.decode_fp8_step, W.decode_fp8_attn], None
-    else:
-        W.setup_reshape(rank)
-        ph, fl = [W.reshape4], None
-    t = timed_loop(torch, args.steps, args.warmup, ph, flush=fl)
-    print(json.dumps({"only": args.only, "ms_per_phase": [sum(x) / len(x) for x in t]}))
+    def verify(self):
+        torch, dev = self.torch, self.dev
+        bf = torch.bfloat16
+        res = {}
+        # prefill: rows at the start, middle and end of each sequence, all 64 heads
+        loc = [0, 64, self.L // 2, self.L // 2 + 64, self.L - 64]
+        pos = torch.cat([torch.arange(a, a + 64) for a in loc[::2]] +
+                        [torch.arange(loc[1], loc[1] + 64)]).to(dev)
+        rows = torch.cat([pos + b * self.L for b in range(self.NSEQ)])
+        got = self._gather_heads(self.out[rows])
+        if self.dd.rank == 0:
+            allq, allk = list(range(self.HQ)), list(range(self.HKV))
+            q = per_head_randn(torch, (self.tot, D), allq, self.SEED_Q, dev, bf)
+            k = per_head_randn(torch, (self.tot, D), allk, self.SEED_K, dev, bf)
+            v = per_head_randn(torch, (self.tot, D), allk, self.SEED_V, dev, bf)
+            refs = []
+            for b in range(self.NSEQ):
+                sl = slice(b * self.L, (b + 1) * self.L)
+                refs.append(torch_attention_rows(torch, q[sl][pos], pos, k[sl], v[sl],
+                                                 self.HQ // self.HKV, D ** -0.5))
+            res["prefill"] = dict(err_stats(torch, got, torch.cat(refs)),
+                                  rows=int(rows.numel()), heads=self.HQ)
+            del q, k, v
+        # decode: 8 sampled sequences, all 64 heads
+        if hasattr(self, "dq"):
+            sample = torch.randperm(self.dB, generator=torch.Generator().manual_seed(44))[:8]
+            got = self._gather_heads(self.dout[sample.to(dev)])
+            if self.dd.rank == 0:
+                allq, allk = list(range(self.HQ)), list(range(self.HKV))
+                dq = per_head_randn(torch, (self.dB, D), allq, self.SEED_DQ, dev, bf)
+                nk = per_head_randn(torch, (self.dB, D), allk, self.SEED_NK, dev, bf)
+                nv = per_head_randn(torch, (self.dB, D), allk, self.SEED_NV, dev, bf)
+                ks, vs = [], []
+                for h in allk:   # one head's cache at a time, only the sampled pages kept
+                    g = torch.Generator(device=dev)
+                    kk, vv = [], []
+                    for seed, dst in ((self.SEED_DK, kk), (self.SEED_DV, vv)):
+                        g.manual_seed(seed + h)
+                        full = torch.randn(self.dpool, BS, D, device=dev, dtype=bf, generator=g)
+                        for b in sample.tolist():
+                            n = int(self.dctx_h[b]) + 1
+                            ids = self.dbt_h[b, :cdiv(n, BS)].long().to(dev)
+                            dst.append(full[ids].reshape(-1, D)[:n].clone())
+                        del full
+                    ks.append(kk)
+                    vs.append(vv)
+                refs = []
+                for i, b in enumerate(sample.tolist()):
+                    n = int(self.dctx_h[b]) + 1
+                    k = torch.stack([ks[h][i] for h in allk], 1)   # [n, Hkv, D]
+                    v = torch.stack([vs[h][i] for h in allk], 1)
+                    k[n - 1], v[n - 1] = nk[b], nv[b]              # the step's new token
+                    refs.append(torch_attention_rows(
+                        torch, dq[b:b + 1], torch.tensor([n - 1], device=dev), k, v,
+                        self.HQ // self.HKV, D ** -0.5))
+                res["decode"] = dict(err_stats(torch, got, torch.cat(refs)),
+                                     sequences=len(sample), heads=self.HQ)
+        return res
 
 
-def run_e2e(W, args, torch, world, max_over_ranks, barrier):
-    """Same metric through the public torch API (tecoops.reshape_and_cache +
-    tecoops.flash_attn_varlen_func) with inputs in pinned host memory: every step
-    copies q, the new K/V, slot_mapping, cu_seqlens_q, seqused_k and block_table
-    host->device and reads the output back device->host.  Steps are pipelined the way
-    a serving loop would run them: step i+1's upload (copy stream), step i's kernels
-    (compute stream) and step i-1's download (second copy stream) overlap, with two
-    sets of device buffers; the timed region spans all K steps, from the first upload
-    to the last download."""
+def run_e2e_prefill(W, args, dd):
+    """The headline prefill step through the public torch API (tecoops.reshape_and_cache
+    + tecoops.flash_attn_varlen_func) with this rank's inputs in pinned host memory:
+    every step copies q, the new K/V, slot_mapping, cu_seqlens_q, seqused_k and
+    block_table host->device and reads the output back device->host.  Steps are
+    pipelined as a serving loop runs them: step i+1's upload (copy stream), step i's
+    kernels (compute stream) and step i-1's download (second copy stream) overlap,
+    with two sets of device buffers; the timed region spans all K steps, from the first
+    upload to the last download, max over ranks."""
     import tecoops
+    torch = W.torch
     host = {n: t.cpu().pin_memory() for n, t in
             (("q", W.q), ("k", W.k), ("v", W.v), ("slot", W.slot), ("bt", W.bt))}
     cu = torch.zeros(len(W.lens) + 1, dtype=torch.int32)
@@ -784,7 +477,7 @@ def run_e2e(W, args, torch, world, max_over_ranks, barrier):
         with torch.cuda.stream(s_comp):
             d = dev[b]
             tecoops.reshape_and_cache(d["k"], d["v"], d["slot"], W.kc, W.vc)
-            tecoops.flash_attn_varlen_func(d["q"], W.kc, W.vc, W.max_q, d["cu"], W.max_q, empty,
+            tecoops.flash_attn_varlen_func(d["q"], W.kc, W.vc, W.L, d["cu"], W.L, empty,
                                            d["seqused"], D ** -0.5, True, empty, d["bt"], False,
                                            out_d[b])
             ev["comp"][b].record(s_comp)
@@ -796,118 +489,630 @@ def run_e2e(W, args, torch, world, max_over_ranks, barrier):
 
     for i in range(args.warmup):
         step(i)
-    torch.cuda.synchronize()
-    barrier()
+    dd.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(s_up)
     for i in range(args.steps):
         step(i)
     t1.record(s_down)
-    torch.cuda.synchronize()
-    barrier()
-    ms = max_over_ranks(t0.elapsed_time(t1))
-    return {"value": world * args.steps * W.flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-            "ms_per_step": ms / args.steps, "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h,
+    dd.barrier()
+    ms = dd.max(t0.elapsed_time(t1))
+    return {"value": args.steps * W.flops_total / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ms / args.steps, "h2d_bytes_per_step": h2d * dd.world,
+            "d2h_bytes_per_step": d2h * dd.world,
+            "per_rank_bytes": {"h2d": h2d, "d2h": d2h},
             "api": "tecoops.reshape_and_cache + tecoops.flash_attn_varlen_func (pinned host "
                    "buffers; upload / kernels / download of consecutive steps overlapped on "
-                   "three streams)"}
+                   "three streams); bytes are the whole job's"}
+
+
+# ----------------------------------------------------------------------------- extras
+class Llama8B:
+    """Llama-3-8B-shaped workloads (Hq 32, Hkv 8, D 128, bf16, bs 16) on one GPU."""
+
+    HQ, HKV = 32, 8
+
+    def __init__(self):
+        import torch
+        from tecoops import capi
+        self.torch, self.capi = torch, capi
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        g = torch.Generator(device=dev).manual_seed(1000)
+        bf = torch.bfloat16
+        self.lens = torch.randint(512, 2049, (4,), generator=torch.Generator().manual_seed(10)).tolist()
+        tot = self.tot = sum(self.lens)
+        self.q = torch.randn(tot, self.HQ, D, device=dev, dtype=bf, generator=g)
+        self.k = torch.randn(tot, self.HKV, D, device=dev, dtype=bf, generator=g)
+        self.v = torch.randn(tot, self.HKV, D, device=dev, dtype=bf, generator=g)
+        pages = [cdiv(n, BS) for n in self.lens]
+        self.nb = sum(pages)
+        bt = torch.zeros(len(self.lens), max(pages), dtype=torch.int32)
+        slots, p0 = [], 0
+        for b, n in enumerate(self.lens):
+            bt[b, :pages[b]] = torch.arange(p0, p0 + pages[b], dtype=torch.int32)
+            slots.append(torch.arange(n) + p0 * BS)
+            p0 += pages[b]
+        self.bt = bt.to(dev)
+        self.slot = torch.cat(slots).to(dev)
+        self.kc = torch.zeros(self.nb, self.HKV, BS, D, device=dev, dtype=bf)
+        self.vc = torch.zeros_like(self.kc)
+        self.qlens = torch.tensor(self.lens, dtype=torch.int32, device=dev)
+        self.out = torch.empty_like(self.q)
+        self.flops = attn_flops(self.lens, self.lens, hq=self.HQ)
+        self.h = capi.Handle(torch.cuda.current_stream().cuda_stream)
+        self.d_bt = capi.Desc(capi.DATA_INT32, self.bt.shape)
+        self.d_q = capi.Desc(capi.DATA_BFLOAT16, self.q.shape)
+        self.d_c = capi.Desc(capi.DATA_BFLOAT16, self.kc.shape)
+        self.max_q = max(self.lens)
+        self.rbytes = reshape_bytes(tot, tot, hkv=self.HKV)
+        self.flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
+
+    def flush(self):
+        self.flush_buf.zero_()
+
+    def reshape(self):
+        self.capi.check(self.capi.reshape_and_cache(
+            self.h, self.k.data_ptr(), self.v.data_ptr(), self.slot.data_ptr(),
+            self.kc.data_ptr(), self.vc.data_ptr(), self.tot, self.HKV, D, self.nb, BS),
+            "reshape_and_cache")
+
+    def prefill(self):
+        self.capi.check(self.capi.flash_attention(
+            self.h, self.max_q, self.max_q, self.nb, self.qlens.data_ptr(), self.qlens.data_ptr(),
+            self.d_bt, self.bt.data_ptr(), self.d_q, self.q.data_ptr(), self.d_c,
+            self.kc.data_ptr(), self.d_c, self.vc.data_ptr(), self.d_q, self.out.data_ptr()),
+            "flash_attention")
+
+    # e4m3 cache: reshape_ex quantises, prefill_ex reads it
+    def setup_fp8(self):
+        torch, capi = self.torch, self.capi
+        self.p8_s = 1.0 / 64
+        self.p8_kc = torch.zeros(self.kc.shape, dtype=torch.uint8, device=self.dev)
+        self.p8_vc = torch.zeros_like(self.p8_kc)
+        self.p8_desc = capi.Desc(capi.DATA_FLOAT8_E4M3, self.p8_kc.shape)
+
+    def reshape_fp8(self):
+        capi = self.capi
+        capi.check(capi.reshape_and_cache_ex(
+            self.h, self.k.data_ptr(), self.v.data_ptr(), self.slot.data_ptr(),
+            self.p8_kc.data_ptr(), self.p8_vc.data_ptr(), self.tot, self.HKV, D, self.nb, BS,
+            capi.DATA_BFLOAT16, cache_dtype=capi.DATA_FLOAT8_E4M3, k_scale=self.p8_s,
+            v_scale=self.p8_s), "reshape_and_cache_ex fp8")
+
+    def prefill_fp8(self):
+        capi = self.capi
+        capi.check(capi.flash_attention_ex(
+            self.h, self.max_q, self.max_q, self.nb, self.qlens.data_ptr(), self.qlens.data_ptr(),
+            self.d_bt, self.bt.data_ptr(), self.d_q, self.q.data_ptr(), self.p8_desc,
+            self.p8_kc.data_ptr(), self.p8_desc, self.p8_vc.data_ptr(), self.d_q,
+            self.out.data_ptr(), k_scale=self.p8_s, v_scale=self.p8_s), "flash_attention_ex fp8")
+
+    # decode: B 64, ctx U{512..8192}, 40k-page pool
+    def setup_decode(self):
+        torch, capi = self.torch, self.capi
+        B, pool = 64, 40000
+        ctx = torch.randint(512, 8193, (B,), generator=torch.Generator().manual_seed(20))
+        perm = torch.randperm(pool, generator=torch.Generator().manual_seed(21)).to(torch.int32)
+        pages = cdiv(ctx + 1, BS).tolist()
+        bt = torch.zeros(B, max(pages), dtype=torch.int32)
+        p0 = 0
+        for b in range(B):
+            bt[b, :pages[b]] = perm[p0:p0 + pages[b]]
+            p0 += pages[b]
+        gd = torch.Generator(device=self.dev).manual_seed(2200)
+        bf = torch.bfloat16
+        self.d_kc = torch.randn(pool, self.HKV, BS, D, device=self.dev, dtype=bf, generator=gd)
+        self.d_vc = torch.randn(pool, self.HKV, BS, D, device=self.dev, dtype=bf, generator=gd)
+        self.d_q3 = torch.randn(B, self.HQ, D, device=self.dev, dtype=bf, generator=gd)
+        self.d_knew = torch.randn(B, self.HKV, D, device=self.dev, dtype=bf, generator=gd)
+        self.d_vnew = torch.randn(B, self.HKV, D, device=self.dev, dtype=bf, generator=gd)
+        slot = [int(bt[b, int(ctx[b]) // BS]) * BS + int(ctx[b]) % BS for b in range(B)]
+        self.d_slot = torch.tensor(slot, dtype=torch.int64, device=self.dev)
+        self.d_ctx = (ctx + 1).to(torch.int32).to(self.dev)
+        self.d_ones = torch.ones(B, dtype=torch.int32, device=self.dev)
+        self.d_bt3 = bt.to(self.dev)
+        self.d_out3 = torch.empty_like(self.d_q3)
+        self.d_desc = (capi.Desc(capi.DATA_INT32, bt.shape),
+                       capi.Desc(capi.DATA_BFLOAT16, self.d_q3.shape),
+                       capi.Desc(capi.DATA_BFLOAT16, self.d_kc.shape))
+        self.d_B, self.d_pool = B, pool
+        self.d_maxk = int(ctx.max()) + 1
+        kv = (ctx + 1).tolist()
+        self.decode_bytes = attn_bytes([1] * B, kv, hq=self.HQ, hkv=self.HKV)
+        self.decode_reshape_bytes = reshape_bytes(B, B, hkv=self.HKV)
+        self.f_bytes = attn_bytes([1] * B, kv, hq=self.HQ, hkv=self.HKV, elem=1)
+        self.f_reshape_bytes = 8 * B + 2 * B * self.HKV * D * 2 + 2 * B * self.HKV * D
+
+    def decode_reshape(self):
+        self.capi.check(self.capi.reshape_and_cache(
+            self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(), self.d_slot.data_ptr(),
+            self.d_kc.data_ptr(), self.d_vc.data_ptr(), self.d_B, self.HKV, D, self.d_pool, BS),
+            "reshape_and_cache")
+
+    def decode(self):
+        bt_d, q_d, c_d = self.d_desc
+        self.capi.check(self.capi.flash_attention(
+            self.h, 1, self.d_maxk, self.d_pool, self.d_ones.data_ptr(), self.d_ctx.data_ptr(),
+            bt_d, self.d_bt3.data_ptr(), q_d, self.d_q3.data_ptr(), c_d, self.d_kc.data_ptr(),
+            c_d, self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr()), "flash_attention")
+
+    def decode_fused(self):
+        bt_d, q_d, c_d = self.d_desc
+        self.capi.check(self.capi.reshape_and_cache_flash_attention_decode(
+            self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(), self.d_slot.data_ptr(),
+            self.d_maxk, self.d_ones.data_ptr(), self.d_ctx.data_ptr(), bt_d,
+            self.d_bt3.data_ptr(), q_d, self.d_q3.data_ptr(), c_d, self.d_kc.data_ptr(), c_d,
+            self.d_vc.data_ptr(), q_d, self.d_out3.data_ptr()), "fused decode")
+
+    def setup_decode_fp8(self):
+        torch, capi = self.torch, self.capi
+        self.f_s = 1.0 / 64
+        self.f_kc = (self.d_kc.float() / self.f_s).to(torch.float8_e4m3fn).view(torch.uint8)
+        self.f_vc = (self.d_vc.float() / self.f_s).to(torch.float8_e4m3fn).view(torch.uint8)
+        self.f_desc = capi.Desc(capi.DATA_FLOAT8_E4M3, self.f_kc.shape)
+
+    def decode_reshape_fp8(self):
+        capi = self.capi
+        capi.check(capi.reshape_and_cache_ex(
+            self.h, self.d_knew.data_ptr(), self.d_vnew.data_ptr(), self.d_slot.data_ptr(),
+            self.f_kc.data_ptr(), self.f_vc.data_ptr(), self.d_B, self.HKV, D, self.d_pool, BS,
+            capi.DATA_BFLOAT16, cache_dtype=capi.DATA_FLOAT8_E4M3, k_scale=self.f_s,
+            v_scale=self.f_s), "reshape_and_cache_ex fp8")
+
+    def decode_fp8(self):
+        capi = self.capi
+        bt_d, q_d, _ = self.d_desc
+        capi.check(capi.flash_attention_ex(
+            self.h, 1, self.d_maxk, self.d_pool, self.d_ones.data_ptr(), self.d_ctx.data_ptr(),
+            bt_d, self.d_bt3.data_ptr(), q_d, self.d_q3.data_ptr(), self.f_desc,
+            self.f_kc.data_ptr(), self.f_desc, self.f_vc.data_ptr(), q_d, self.d_out3.data_ptr(),
+            k_scale=self.f_s, v_scale=self.f_s), "flash_attention_ex fp8")
+
+
+class ReshapeSweep:
+    """reshape_and_cache into a 65,536-page bf16 cache (Hkv 8, D 128, bs 16, 2 GiB per
+    cache), T new tokens with scattered (random permutation, seed 30) or sequential
+    slots and 0 % / 10 % of them -1 (seed 31)."""
+
+    NB, HKV = 65536, 8
+
+    def __init__(self):
+        import torch
+        from tecoops import capi
+        self.torch, self.capi = torch, capi
+        dev = self.dev = torch.device("cuda", torch.cuda.current_device())
+        bf = torch.bfloat16
+        g = torch.Generator(device=dev).manual_seed(3000)
+        self.kc = torch.zeros(self.NB, self.HKV, BS, D, device=dev, dtype=bf)
+        self.vc = torch.zeros_like(self.kc)
+        self.k = torch.randn(65536, self.HKV, D, device=dev, dtype=bf, generator=g)
+        self.v = torch.randn(65536, self.HKV, D, device=dev, dtype=bf, generator=g)
+        self.perm = torch.randperm(self.NB * BS, generator=torch.Generator().manual_seed(30))
+        self.h = capi.Handle(torch.cuda.current_stream().cuda_stream)
+        self.flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
+
+    def slots(self, T, scattered, pad):
+        torch = self.torch
+        s = self.perm[:T].clone() if scattered else torch.arange(T)
+        n_valid = T
+        if pad > 0:
+            m = torch.rand(T, generator=torch.Generator().manual_seed(31)) < pad
+            s[m] = -1
+            n_valid = int((~m).sum())
+        return s.to(torch.int64).to(self.dev), n_valid
+
+    def run(self, T, slot, steps, warmup):
+        def f():
+            self.capi.check(self.capi.reshape_and_cache(
+                self.h, self.k.data_ptr(), self.v.data_ptr(), slot.data_ptr(), self.kc.data_ptr(),
+                self.vc.data_ptr(), T, self.HKV, D, self.NB, BS), "reshape_and_cache")
+        # inputs below L2 size are flushed between steps
+        fl = (lambda: self.flush_buf.zero_()) if T * self.HKV * D * 2 * 2 < 256e6 else None
+        (t,) = timed_loop(self.torch, steps, warmup, [f], flush=fl)
+        return trimmed_mean(t)
+
+
+def cfg1_pair(torch, capi, steps, warmup):
+    """The CPU-runnable fp16 pair on the GPU: reshape_and_cache T 256 (H 8, D 128,
+    64 pages x 16, slots randperm(1024)[:256] with ~5 % -1) + causal prefill B 1,
+    L = S = 256, Hq = Hkv = 8 (the prefill reads K/V from a 16-page region of the
+    cache written by reshape)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    f16 = torch.float16
+    g = torch.Generator(device=dev).manual_seed(1)
+    H, T, NB = 8, 256, 64
+    key = torch.randn(T, H, D, device=dev, dtype=f16, generator=g)
+    val = torch.randn(T, H, D, device=dev, dtype=f16, generator=g)
+    slot = torch.randperm(NB * BS, generator=torch.Generator().manual_seed(2))[:T]
+    slot[torch.rand(T, generator=torch.Generator().manual_seed(3)) < 0.05] = -1
+    slot = slot.to(torch.int64).to(dev)
+    n_valid = int((slot >= 0).sum())
+    kc = torch.zeros(NB, H, BS, D, device=dev, dtype=f16)
+    vc = torch.zeros_like(kc)
+    q = torch.randn(T, H, D, device=dev, dtype=f16, generator=g)
+    bt = torch.randperm(NB, generator=torch.Generator().manual_seed(5))[:16].to(torch.int32)
+    pslot = (bt.long()[torch.arange(T) // BS] * BS + torch.arange(T) % BS).to(dev)
+    bt = bt.view(1, 16).to(dev)
+    lens = torch.tensor([T], dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    h = capi.Handle(torch.cuda.current_stream().cuda_stream)
+    dbt, dq, dc = (capi.Desc(capi.DATA_INT32, bt.shape), capi.Desc(capi.DATA_HALF, q.shape),
+                   capi.Desc(capi.DATA_HALF, kc.shape))
+    flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev)
+
+    def reshape():
+        capi.check(capi.reshape_and_cache(h, key.data_ptr(), val.data_ptr(), slot.data_ptr(),
+                                          kc.data_ptr(), vc.data_ptr(), T, H, D, NB, BS), "rc")
+
+    def reshape_p():
+        capi.check(capi.reshape_and_cache(h, key.data_ptr(), val.data_ptr(), pslot.data_ptr(),
+                                          kc.data_ptr(), vc.data_ptr(), T, H, D, NB, BS), "rc")
+
+    def prefill():
+        capi.check(capi.flash_attention(h, T, T, NB, lens.data_ptr(), lens.data_ptr(), dbt,
+                                        bt.data_ptr(), dq, q.data_ptr(), dc, kc.data_ptr(), dc,
+                                        vc.data_ptr(), dq, out.data_ptr()), "fa")
+
+    tr, = timed_loop(torch, steps, warmup, [reshape], flush=lambda: flush_buf.zero_())
+    tp = timed_loop(torch, steps, warmup, [reshape_p, prefill], flush=lambda: flush_buf.zero_())
+    fl = attn_flops([T], [T], hq=H)
+    return {"workload": "CPU-runnable fp16 pair on the GPU: reshape_and_cache T 256 (H 8, D 128, "
+                        "64 x 16 pages, randperm slots, ~5 % -1) and causal prefill B 1, L 256, "
+                        "8/8 heads (reshape of its K/V + prefill per step)",
+            "reshape_us": trimmed_mean(tr) * 1e3,
+            "reshape_gbs": reshape_bytes(n_valid, T, hkv=H) / (trimmed_mean(tr) * 1e-3) / 1e9,
+            "prefill_step_us": step_ms(tp) * 1e3,
+            "prefill_kernel_us": trimmed_mean(tp[1]) * 1e3,
+            "prefill_tflops": fl / (trimmed_mean(tp[1]) * 1e-3) / 1e12,
+            "l2": "flushed between steps (inputs < L2); latency-bound at this size"}
 
 
 # ----------------------------------------------------------------------------- CPU arm
-def cpu_prefill_sample(L, rng):
-    """One config-2 sequence of length L on the host: the C reshape loop and the
-    numpy fp32 attention of the oracle (restatements of the reference goldens).
-    Returns (flops, seconds)."""
+def _ref_golden():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import install_ref
+    return install_ref.load_golden()
+
+
+def cpu_sample_70b(golden, b_idx, kv_head, rows=2048, threads=None):
+    """One bounded sample of the headline prefill on the host: the reference golden
+    (torch fp32) for the last `rows` query rows of one 8192-token sequence and the 8 Q
+    heads of one KV head (a chunked prefill of `rows` rows over 8192 keys, which the
+    golden handles natively), preceded by reshape_and_cache of that head's 8192 tokens
+    with the C restatement of the reference loop.  Returns (algorithmic flops, s)."""
     import numpy as np
+    import torch
 
     import oracle
-    q = rng.standard_normal((L, HQ, D), dtype=np.float32).astype(np.float16)
-    k = rng.standard_normal((L, HKV, D), dtype=np.float32).astype(np.float16).view(np.uint16)
-    v = rng.standard_normal((L, HKV, D), dtype=np.float32).astype(np.float16).view(np.uint16)
+    if threads:
+        torch.set_num_threads(threads)
+    L, g = Llama70B.L, Llama70B.HQ // Llama70B.HKV
+    gen = torch.Generator().manual_seed(7000 + 16 * b_idx + kv_head)
+    q = torch.randn(rows, g, D, generator=gen).to(torch.bfloat16)
+    k = torch.randn(L, 1, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(L, 1, D, generator=gen).to(torch.bfloat16)
     nb = cdiv(L, BS)
-    kc = np.zeros((nb, HKV, BS, D), dtype=np.uint16)
+    kc = np.zeros((nb, 1, BS, D), dtype=np.uint16)
     vc = np.zeros_like(kc)
+    kw = k.view(torch.int16).numpy().view(np.uint16)
+    vw = v.view(torch.int16).numpy().view(np.uint16)
     slot = np.arange(L, dtype=np.int64)
-    bt = np.arange(nb, dtype=np.int32)[None]
+    bt = torch.arange(nb, dtype=torch.int32)[None]
     t0 = time.perf_counter()
-    oracle.reshape_and_cache(k, v, slot, kc, vc)
-    oracle.flash_attn_varlen(q.astype(np.float32), kc.view(np.float16).astype(np.float32),
-                             vc.view(np.float16).astype(np.float32), [L], [L], bt)
-    return attn_flops([L], [L]), time.perf_counter() - t0
+    oracle.reshape_and_cache(kw, vw, slot, kc, vc)
+    # the golden's input conversion (python_api_test/test_flash_attention.py:167-181):
+    # 16-bit -> fp32, cache [NB, H, bs, D] -> [NB, bs, H, D]
+    kf = torch.from_numpy(kc.view(np.int16)).view(torch.bfloat16).float().permute(0, 2, 1, 3)
+    vf = torch.from_numpy(vc.view(np.int16)).view(torch.bfloat16).float().permute(0, 2, 1, 3)
+    golden(q.float(), kf.contiguous(), vf.contiguous(), [rows], [L], bt)
+    return attn_flops([rows], [L], hq=g), time.perf_counter() - t0
 
 
-def cpu_baseline_prefill(lens, budget_s=15.0):
-    """Reported CPU baseline: as many config-2 sequences as fit in ~budget_s."""
-    import numpy as np
-    rng = np.random.default_rng(5)
-    flops, secs, used = 0, 0.0, []
-    for L in sorted(lens):
-        f, t = cpu_prefill_sample(L, rng)
-        flops, secs = flops + f, secs + t
-        used.append(L)
-        if secs > budget_s:
+def cpu_baseline_70b(budget_s=15.0):
+    """Reported CPU baseline of the headline: as many bounded samples as fit in
+    ~budget_s (at least one), the reference golden if installed, else not reported."""
+    try:
+        golden = _ref_golden()
+    except ImportError as e:
+        return {"value": None, "unavailable": str(e)}
+    import torch
+    threads = os.cpu_count() or 1
+    flops, secs, n = 0, 0.0, 0
+    cpu_sample_70b(golden, 0, 0, threads=threads)   # warm-up (allocator, thread pool)
+    while n == 0 or secs < budget_s:
+        f, t = cpu_sample_70b(golden, n % 2, n % 8, threads=threads)
+        flops, secs, n = flops + f, secs + t, n + 1
+        if n >= 16:
             break
-    return {"value": flops / secs / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(),
-            "kind": "port",
-            "sample": f"config-2 sequences of lengths {used} (reshape C loop + numpy fp32 "
-                      f"attention), {secs:.1f} s on the host, numpy BLAS on all cores"}
+    return {"value": flops / secs / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "reference",
+            "sample": f"{n} samples of the headline prefill, each the last 2048 query rows of "
+                      "one 8192-token sequence x the 8 Q heads of one KV head over all 8192 keys "
+                      "(the reference golden flash_attn_varlen_func, torch fp32, from "
+                      "baseline/_ref; reshape_and_cache of that head's 8192 tokens by the C "
+                      f"restatement of the reference loop): {secs:.1f} s on the host"}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return   # under torchrun only rank 0 times the CPU path
-    import numpy as np
-    lens = config2_lens()
-    order = sorted(lens)
-    rng = np.random.default_rng(5)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    try:
+        golden = _ref_golden()
+    except ImportError as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference golden not "
+                          f"installed ({e})"}), flush=True)
+        return
+    import torch
+    threads = os.cpu_count() or 1
     flops, secs = 0, 0.0
     for s in range(args.warmup + args.steps):
-        f, t = cpu_prefill_sample(order[s % len(order)], rng)
+        f, t = cpu_sample_70b(golden, s % 2, s % 8, threads=threads)
         if s >= args.warmup:
             flops, secs = flops + f, secs + t
     value = flops / secs / 1e12
-    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
         "impl": "reference", "metric": "prefill TFLOP/s", "value": value, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32 (reference CPU golden)", "data": "synthetic",
-        "config": {"workload": "config 2, one sequence per step rotating over its 4 sequences "
-                               "(bounded sample)", "seq_lens": lens},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": os.cpu_count(),
-                         "kind": "port",
-                         "sample": "each step: one config-2 sequence, reshape_and_cache C loop + "
-                                   "numpy fp32 attention (oracle restatement of the reference "
-                                   "goldens; the reference's SDAA kernels cannot run here)"},
+        "config": {"workload": "Llama-3-70B-shaped causal prefill (Hq 64, Hkv 8, D 128, 2 x 8192 "
+                               "tokens, reshape_and_cache + attention); each step a bounded "
+                               "sample of it", "same_config": True},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "reference",
+                         "sample": "each step: the last 2048 query rows of one 8192-token "
+                                   "sequence x the 8 Q heads of one KV head over all 8192 keys, "
+                                   "through the reference's own golden flash_attn_varlen_func "
+                                   "(test/zoo/teco/flash_attention/flash_attention.py:79-140, "
+                                   "torch fp32, unmodified copy in baseline/_ref), after "
+                                   "reshape_and_cache of that head's tokens (C restatement of "
+                                   "the reference loop, reshape_and_cache.cpp:136-147)"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- our arm
+def run_extras(args, peaks, torch):
+    """Single-GPU extra keys of the N=1 line."""
+    ex = {}
+    W = Llama8B()
+    tr, tp = timed_loop(torch, args.steps, args.warmup, [W.reshape, W.prefill], flush=W.flush)
+    k_ms = trimmed_mean(tp)
+    traffic = load_traffic().get("fa_prefill_tcgen05_sm100/config2")
+    ex["llama8b_prefill"] = {
+        "workload": "Llama-3-8B varlen causal prefill, 4 seqs L~U{512..2048} "
+                    f"({'+'.join(map(str, W.lens))} tokens), Hq 32, Hkv 8, D 128, bs 16, bf16; "
+                    "step = reshape_and_cache of all tokens + prefill",
+        "metric": "prefill TFLOP/s", "unit": "TFLOP/s",
+        "value": W.flops / (step_ms([tr, tp]) * 1e-3) / 1e12,
+        "ms_per_step": step_ms([tr, tp]),
+        "reshape_us": trimmed_mean(tr) * 1e3,
+        "reshape_gbs": W.rbytes / (trimmed_mean(tr) * 1e-3) / 1e9,
+        "roofline": {"bound": "tensor", "kernel": "fa_prefill_tcgen05_sm100",
+                     "achieved": W.flops / (k_ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": W.flops / (k_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                     "kernel_us": k_ms * 1e3, "flops_per_launch": W.flops,
+                     "traffic": traffic, "peak_source": "bf16_tflops (burst)"},
+        "l2": "flushed between timed steps (256 MB write)"}
+    W.setup_fp8()
+    fr, fp = timed_loop(torch, args.steps, args.warmup, [W.reshape_fp8, W.prefill_fp8],
+                        flush=W.flush)
+    ex["llama8b_prefill"]["fp8_cache"] = {
+        "api": "tecoopsReshapeAndCacheEx + tecoopsFlashAttentionEx, e4m3 cache (scale 1/64)",
+        "value": W.flops / (step_ms([fr, fp]) * 1e-3) / 1e12, "ms_per_step": step_ms([fr, fp]),
+        "prefill_us": trimmed_mean(fp) * 1e3}
+    W.setup_decode()
+    tr, ta = timed_loop(torch, args.steps, args.warmup, [W.decode_reshape, W.decode])
+    (tf,) = timed_loop(torch, args.steps, args.warmup, [W.decode_fused])
+    W.setup_decode_fp8()
+    fr, fa = timed_loop(torch, args.steps, args.warmup, [W.decode_reshape_fp8, W.decode_fp8])
+    a_ms, s_ms = trimmed_mean(ta), step_ms([tr, ta])
+    step_bytes = W.decode_bytes + W.decode_reshape_bytes
+    ex["llama8b_decode"] = {
+        "workload": "Llama-3-8B paged decode: B 64, ctx U{512..8192}+1, 40k-page pool, bs 16, "
+                    "bf16; step = reshape_and_cache of the 64 new tokens + split-KV decode",
+        "metric": "decode HBM GB/s", "unit": "GB/s",
+        "value": step_bytes / (s_ms * 1e-3) / 1e9, "ms_per_step": s_ms,
+        "attn_kernel_us": a_ms * 1e3,
+        "attn_frac_of_measured_hbm": W.decode_bytes / (a_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+        "fused": {"api": "tecoopsReshapeAndCacheFlashAttentionDecode (one launch + merge)",
+                  "ms_per_step": trimmed_mean(tf),
+                  "value": step_bytes / (trimmed_mean(tf) * 1e-3) / 1e9},
+        "fp8_cache": {"api": "tecoopsReshapeAndCacheEx + tecoopsFlashAttentionEx, e4m3 cache",
+                      "ms_per_step": step_ms([fr, fa]),
+                      "attn_kernel_us": trimmed_mean(fa) * 1e3,
+                      "attn_frac_of_measured_hbm": W.f_bytes / (trimmed_mean(fa) * 1e-3) / 1e9
+                      / peaks["hbm_gbs"],
+                      "speedup_vs_bf16_step": s_ms / step_ms([fr, fa])},
+        "l2": "inputs (1.1 GB of K/V) larger than L2"}
+    del W
+    torch.cuda.empty_cache()
+    R = ReshapeSweep()
+    sweep = []
+    for T in (1, 16, 256, 4096, 65536):
+        for scattered in (True, False):
+            for pad in (0.0, 0.1):
+                slot, nv = R.slots(T, scattered, pad)
+                ms = R.run(T, slot, args.steps, args.warmup)
+                by = reshape_bytes(nv, T, hkv=R.HKV)
+                sweep.append({"T": T, "slots": "scattered" if scattered else "sequential",
+                              "pad": pad, "us": ms * 1e3, "bytes": by,
+                              "gbs": by / (ms * 1e-3) / 1e9,
+                              "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]})
+    ex["reshape_sweep"] = {
+        "workload": "reshape_and_cache into a 65,536-page bf16 cache (Hkv 8, D 128, bs 16, 2 GiB "
+                    "per cache); bytes 8*T + 4*valid*Hkv*D*2; L2 flushed between steps when the "
+                    "inputs are below 256 MB",
+        "metric": "reshape_and_cache HBM GB/s", "unit": "GB/s", "points": sweep}
+    del R
+    torch.cuda.empty_cache()
+    from tecoops import capi
+    ex["fp16_pair"] = cfg1_pair(torch, capi, args.steps, args.warmup)
+    ex["rms_norm"] = run_rms(args, peaks, torch)
+    return ex
+
+
+def run_rms(args, peaks, torch):
+    from tecoops import capi
+    dev = torch.device("cuda", torch.cuda.current_device())
+    nT, hidden = 97056, 4096
+    g = torch.Generator(device=dev).manual_seed(4000)
+    bf = torch.bfloat16
+    x = torch.randn(nT, hidden, device=dev, dtype=bf, generator=g)
+    r = torch.randn(nT, hidden, device=dev, dtype=bf, generator=g)
+    w = torch.randn(hidden, device=dev, dtype=bf, generator=g)
+    y, ro = torch.empty_like(x), torch.empty_like(x)
+    nbytes = nT * hidden * 2 * 4 + hidden * 2
+    h = capi.Handle(torch.cuda.current_stream().cuda_stream)
+
+    def f():
+        capi.check(capi.rms_norm(h, x.data_ptr(), w.data_ptr(), r.data_ptr(), y.data_ptr(),
+                                 ro.data_ptr(), nT, hidden, 1e-6, dtype=capi.DATA_BFLOAT16), "rms")
+    (t,) = timed_loop(torch, args.steps, args.warmup, [f])
+    ms = trimmed_mean(t)
+    return {"workload": f"rms_norm with residual add, {nT} tokens x hidden 4096, bf16",
+            "metric": "rms_norm HBM GB/s", "unit": "GB/s", "value": nbytes / (ms * 1e-3) / 1e9,
+            "kernel_us": ms * 1e3, "frac_of_measured_hbm": nbytes / (ms * 1e-3) / 1e9
+            / peaks["hbm_gbs"], "l2": f"inputs ({nbytes / 1e6:.0f} MB) larger than L2"}
+
+
+def run_ours(args):
+    dd = Dist()
+    import torch
+    peaks, peak_src = load_peaks()
+    if args.only:
+        run_only(args, dd, torch)
+        dd.close()
+        return
+    W = Llama70B(dd)
+    clocks = ClockSampler(dd.local)
+    dd.barrier()
+    clocks.start()
+    # ---- headline: prefill step (reshape + prefill) of this rank's heads
+    tr, tp = timed_loop(torch, args.steps, args.warmup, [W.reshape, W.prefill], flush=W.flush)
+    dd.barrier()
+    ms = dd.max(step_ms([tr, tp]))
+    k_ms = trimmed_mean(tp)
+    value = W.flops_total / (ms * 1e-3) / 1e12
+    achieved = W.flops_local / (k_ms * 1e-3) / 1e12
+    k_ms_max = dd.max(k_ms)
+    # ---- decode step of the same shards
+    td, ta = timed_loop(torch, args.steps, args.warmup, [W.decode_reshape, W.decode])
+    dd.barrier()
+    dms = dd.max(step_ms([td, ta]))
+    da_ms = trimmed_mean(ta)
+    clk = clocks.stop()
+    e2e = run_e2e_prefill(W, args, dd)
+    verify = W.verify()
+    del W.dkc, W.dvc
+    torch.cuda.empty_cache()
+    extras = {}
+    if dd.world == 1 and not args.no_extras:
+        clocks2 = ClockSampler(dd.local)
+        clocks2.start()
+        extras = run_extras(args, peaks, torch)
+        extras["clocks"] = clocks2.stop()
+    cpu = None
+    if dd.rank == 0 and dd.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_70b(budget_s=args.cpu_budget)
+    if dd.rank == 0:
+        traffic = load_traffic().get(f"fa_prefill_tcgen05_sm100/llama70b_n{dd.world}")
+        line = {
+            "metric": "prefill TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": dd.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) Q/K/V per head, Llama-3-70B head shapes)",
+            "config": {"workload": "Llama-3-70B-shaped attention sharded by KV head: Hq 64, Hkv 8, "
+                                   "D 128, bf16, bs 16; prefill step = reshape_and_cache of "
+                                   "2 x 8192 tokens + causal prefill",
+                       "seq_lens": W.lens,
+                       "parallelism": f"KV heads split over {dd.world} GPU(s): "
+                                      f"{W.hkv} KV / {W.hq} Q heads per rank, no collective",
+                       "l2": "flushed between timed prefill steps (256 MB write)",
+                       "timing": "per-step CUDA events, 10 %-trimmed mean of K steps, max over "
+                                 "ranks"},
+            "gpu_launches": 2 * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "fa_prefill_tcgen05_sm100",
+                         "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_tflops"],
+                         "peak_source": f"{peak_src} bf16_tflops (burst)",
+                         "traffic": traffic, "flops_per_launch": W.flops_local,
+                         "kernel_us": k_ms * 1e3, "kernel_us_max_over_ranks": k_ms_max * 1e3},
+            "reshape_us_per_step": trimmed_mean(tr) * 1e3,
+            "decode": {"workload": "Llama-3-70B-shaped paged decode sharded by KV head: B 256, "
+                                   "ctx U{1024..32768}+1, bs 16, random block tables; step = "
+                                   "reshape_and_cache of the 256 new tokens + split-KV decode",
+                       "metric": "decode HBM GB/s", "unit": "GB/s",
+                       "value": W.dbytes_total / (dms * 1e-3) / 1e9, "ms_per_step": dms,
+                       "attn_kernel_us": da_ms * 1e3,
+                       "per_gpu_attn_frac_of_measured_hbm":
+                           W.d_attn_bytes_local / (da_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                       "l2": f"inputs ({W.dbytes_local / 1e9:.1f} GB per GPU) larger than L2"},
+            "e2e": e2e,
+            "verify": verify,
+            "clocks": clk,
+        }
+        line.update(extras)
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    dd.close()
+
+
+def run_only(args, dd, torch):
+    """One workload's timed loop only (profiler captures run this)."""
+    if args.only in ("prefill70b", "decode70b"):
+        W = Llama70B(dd, with_decode=args.only == "decode70b")
+        ph, fl = ([W.reshape, W.prefill], W.flush) if args.only == "prefill70b" else \
+            ([W.decode_reshape, W.decode], None)
+    elif args.only in ("prefill8b", "prefill8b_fp8"):
+        W = Llama8B()
+        if args.only == "prefill8b":
+            ph, fl = [W.reshape, W.prefill], W.flush
+        else:
+            W.setup_fp8()
+            ph, fl = [W.reshape_fp8, W.prefill_fp8], W.flush
+    elif args.only in ("decode8b", "decode8b_fp8"):
+        W = Llama8B()
+        W.setup_decode()
+        ph, fl = [W.decode_reshape, W.decode], None
+        if args.only == "decode8b_fp8":
+            W.setup_decode_fp8()
+            ph = [W.decode_reshape_fp8, W.decode_fp8]
+    elif args.only.startswith("reshape"):
+        R = ReshapeSweep()
+        T = int(args.only[len("reshape"):] or 65536)
+        slot, _ = R.slots(T, True, 0.0)
+        print(json.dumps({"only": args.only, "us": R.run(T, slot, args.steps, args.warmup) * 1e3}))
+        return
+    else:
+        raise SystemExit(f"unknown --only {args.only}")
+    t = timed_loop(torch, args.steps, args.warmup, ph, flush=fl)
+    print(json.dumps({"only": args.only, "ms_per_phase": [trimmed_mean(x) for x in t]}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--workload", choices=["config2", "70b"], default="config2",
-                    help="config2 (default headline, weak scaling) or 70b (config 5, "
-                         "KV-head sharded, strong scaling)")
-    ap.add_argument("--only", choices=["prefill", "decode", "decode_fp8", "reshape", "rms_norm"], default=None,
-                    help="run one workload's timed loop only (for profiler captures); "
-                         "prints a reduced JSON line")
+    ap.add_argument("--only", default=None,
+                    help="one workload's timed loop (prefill70b, decode70b, prefill8b, "
+                         "prefill8b_fp8, decode8b, decode8b_fp8, reshape<T>)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "70b":
-        run_70b(args)
     else:
         run_ours(args)
 

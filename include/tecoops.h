@@ -339,8 +339,10 @@ tecoopsStatus_t tecoopsGetDeviceErrorStatus(tecoopsHandle_t handle, int *error_c
  * wait of the split-KV decode kernel launched through this handle (default
  * 2,000,000,000 ns; 0 is BAD_PARAM).  stall_test != 0 makes the first ring wait of
  * each consumer warp wait on a barrier that nothing completes, so that the wait runs
- * out after limit_ns, records its site (0x12nn), and the kernel drains its copies
- * and returns; the host then reads the code with tecoopsGetDeviceErrorStatus.
+ * out after limit_ns (and with it the producer's wait for the stage that consumer
+ * holds); the first wait to give up records its site (0x12nn or 0x11nn), and the
+ * kernel drains its copies and returns; the host then reads the code with
+ * tecoopsGetDeviceErrorStatus.
  * Nothing faults, traps or waits without a bound.  stall_test = 0 restores normal
  * operation.
  */

@@ -14,8 +14,12 @@
 // loads issued before any store (memory-level parallelism), loads bypass L1
 // (read-once data), consecutive lanes touch consecutive 16-byte pieces of the
 // same 256-byte head row, so both the reads and the scattered writes are whole
-// 32-byte sectors.  The grid is a multiple of the SM count.  64-bit offsets
-// throughout (caches beyond 2^31 elements).
+// 32-byte sectors.  The K/V loads do not wait for the slot_mapping load (only the
+// stores need the slot), so a pass costs one DRAM round trip, not two; a launch
+// that fits in 8 CTAs of 256 per SM takes one pass with every load in flight at
+// once (2 vectors per thread below half that size), larger ones stride over a
+// grid of 8 CTAs per SM.  64-bit offsets throughout (caches beyond 2^31
+// elements).
 //
 // Extensions: the cache strides cover both page layouts ([NB, H, bs, D] and
 // vLLM's [NB, bs, H, D]); an e4m3 cache stores e4m3(x / scale) with IEEE division
@@ -76,15 +80,14 @@ __global__ void __launch_bounds__(256) reshape_and_cache_vec16_kernel(
                 const int h = r / vecs_per_head;
                 const int c = r - h * vecs_per_head;
                 const int64_t slot = __ldg(slot_mapping + t);
+                // K/V loads independent of the slot: in flight with the slot load
+                kv[u] = ld_stream16(key + t * key_stride_b + (int64_t)r * 16);
+                vv[u] = ld_stream16(value + t * value_stride_b + (int64_t)r * 16);
                 if (slot >= 0 && slot < num_slots) {
                     const int64_t blk = slot / block_size;
                     const int64_t off = slot - blk * block_size;
                     dst[u] = blk * block_stride_b + h * head_stride_b + off * entry_stride_b +
                              (int64_t)c * 16;
-                    const int64_t srck = t * key_stride_b + (int64_t)r * 16;
-                    const int64_t srcv = t * value_stride_b + (int64_t)r * 16;
-                    kv[u] = ld_stream16(key + srck);
-                    vv[u] = ld_stream16(value + srcv);
                 }
             }
         }
@@ -270,16 +273,18 @@ cudaError_t launch_reshape_and_cache(const ReshapeAndCacheArgs &a, int num_sms,
                      aligned16(a.key_cache) && aligned16(a.value_cache) &&
                      ((a.key_stride * eb) % 16 == 0) && ((a.value_stride * eb) % 16 == 0);
     if (vec) {
-        constexpr int kUnroll = 4;
         const int vecs_per_head = row_bytes / 16;
         const int64_t total = (int64_t)a.num_tokens * a.num_kv_heads * vecs_per_head;
         const int threads = 256;
-        int64_t want = (total + (int64_t)threads * kUnroll - 1) / ((int64_t)threads * kUnroll);
         const int64_t cap = (int64_t)num_sms * 8;   // 8 resident CTAs of 256 per SM
-        int64_t grid = want < cap ? want : cap;
-        if (grid >= num_sms) grid = (grid / num_sms) * num_sms;   // whole waves
-        if (grid < 1) grid = 1;
-        reshape_and_cache_vec16_kernel<kUnroll><<<(unsigned)grid, threads, 0, stream>>>(
+        // one pass when everything fits in the resident CTAs: 2 vectors per thread
+        // (twice the CTAs) below half of that, 4 otherwise; larger T strides
+        const bool small = total <= cap * threads * 2;
+        const int unroll = small ? 2 : 4;
+        const int64_t want = (total + (int64_t)threads * unroll - 1) / ((int64_t)threads * unroll);
+        const int64_t grid = want < 1 ? 1 : (want < cap ? want : cap);
+        auto kfn = small ? reshape_and_cache_vec16_kernel<2> : reshape_and_cache_vec16_kernel<4>;
+        kfn<<<(unsigned)grid, threads, 0, stream>>>(
             static_cast<const uint8_t *>(a.key), static_cast<const uint8_t *>(a.value),
             a.slot_mapping, static_cast<uint8_t *>(a.key_cache),
             static_cast<uint8_t *>(a.value_cache), total, vecs_per_head, a.num_kv_heads,

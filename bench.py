@@ -200,7 +200,7 @@ def step_ms(times):
 
 
 class Dist:
-    def __init__(self):
+    def __init__(self, shard_of=0):
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
@@ -210,6 +210,8 @@ class Dist:
         torch.cuda.set_device(self.local)
         if self.world > 1:
             dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+        self.shard_world = shard_of or self.world   # --shard-of: rank 0's shard of an N-way
+                                                    # split, alone on one GPU (analysis)
 
     def barrier(self):
         if self.world > 1:
@@ -272,7 +274,8 @@ class Llama70B:
         self.torch, self.capi, self.dd = torch, capi, dd
         dev = torch.device("cuda", torch.cuda.current_device())
         self.dev = dev
-        self.shard = s = sharding.head_shard(self.HQ, self.HKV, dd.world, dd.rank)
+        self.shard = s = sharding.head_shard(self.HQ, self.HKV, dd.shard_world,
+                                             dd.rank if dd.shard_world == dd.world else 0)
         self.hq, self.hkv = s.q_heads, s.kv_heads
         self.qh = list(range(s.q_begin, s.q_end))
         self.kh = list(range(s.kv_begin, s.kv_end))
@@ -981,7 +984,27 @@ def run_rms(args, peaks, torch):
             / peaks["hbm_gbs"], "l2": f"inputs ({nbytes / 1e6:.0f} MB) larger than L2"}
 
 
+def run_shard_of(args):
+    """Rank 0's share of an N-way KV-head split of the headline, alone on one GPU (no
+    process group): the per-rank prefill and decode kernel times that bound the N-GPU
+    step, for analysing the scaling curve without holding N GPUs."""
+    dd = Dist(shard_of=args.shard_of)
+    import torch
+    W = Llama70B(dd)
+    tr, tp = timed_loop(torch, args.steps, args.warmup, [W.reshape, W.prefill], flush=W.flush)
+    td, ta = timed_loop(torch, args.steps, args.warmup, [W.decode_reshape, W.decode])
+    print(json.dumps({"shard_of": args.shard_of, "kv_heads": W.hkv, "q_heads": W.hq,
+                      "prefill_step_ms": step_ms([tr, tp]), "prefill_kernel_us": trimmed_mean(tp) * 1e3,
+                      "reshape_us": trimmed_mean(tr) * 1e3,
+                      "prefill_tflops_per_gpu": W.flops_local / (trimmed_mean(tp) * 1e-3) / 1e12,
+                      "decode_step_ms": step_ms([td, ta]), "decode_kernel_us": trimmed_mean(ta) * 1e3,
+                      "decode_gbs_per_gpu": W.d_attn_bytes_local / (trimmed_mean(ta) * 1e-3) / 1e9}))
+
+
 def run_ours(args):
+    if args.shard_of:
+        run_shard_of(args)
+        return
     dd = Dist()
     import torch
     peaks, peak_src = load_peaks()
@@ -1021,7 +1044,10 @@ def run_ours(args):
     if dd.rank == 0 and dd.world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_70b(budget_s=args.cpu_budget)
     if dd.rank == 0:
-        traffic = load_traffic().get(f"fa_prefill_tcgen05_sm100/llama70b_n{dd.world}")
+        # DRAM bytes of one launch from the committed N=1 ncu capture, scaled by this
+        # rank's share of the heads (traffic is proportional to the heads a rank holds)
+        t1 = load_traffic().get("fa_prefill_tcgen05_sm100/llama70b_n1")
+        traffic = t1 * W.flops_local / W.flops_total if t1 else None
         line = {
             "metric": "prefill TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": dd.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -1105,6 +1131,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="analysis: time rank 0's shard of an N-way KV-head split on one GPU")
     ap.add_argument("--only", default=None,
                     help="one workload's timed loop (prefill70b, decode70b, prefill8b, "
                          "prefill8b_fp8, decode8b, decode8b_fp8, reshape<T>)")

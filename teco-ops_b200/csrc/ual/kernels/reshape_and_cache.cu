@@ -54,40 +54,59 @@ __device__ __forceinline__ void st16(void *p, const uint4 &v) {
                  : "memory");
 }
 
+// Unsigned 32-bit division by a run-time constant d >= 1 for n < 2^31 (round-up
+// reciprocal, Granlund-Montgomery): with s = ceil(log2 d) and
+// magic = floor(2^32 (2^s - d) / d) + 1, n / d = (umulhi(n, magic) + n) >> s; the sum
+// stays below 2^32 because n < 2^31.
+struct FastDiv {
+    uint32_t magic, shift, d;
+};
+static inline FastDiv make_fastdiv(uint32_t d) {
+    uint32_t s = 0;
+    while (s < 32 && (1ull << s) < d) ++s;
+    FastDiv f;
+    f.magic = (uint32_t)((((1ull << 32) * ((1ull << s) - d)) / d) + 1);
+    f.shift = s;
+    f.d = d;
+    return f;
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+    return (__umulhi(n, f.magic) + n) >> f.shift;
+}
+
 // Vectorised path: head_size*2 bytes is a multiple of 16 and every base pointer
-// and token stride is 16-byte aligned.
+// and token stride is 16-byte aligned; fewer than 2^31 vectors (32-bit indices).
 template <int UNROLL>
 __global__ void __launch_bounds__(256) reshape_and_cache_vec16_kernel(
     const uint8_t *__restrict__ key, const uint8_t *__restrict__ value,
     const int64_t *__restrict__ slot_mapping, uint8_t *__restrict__ key_cache,
-    uint8_t *__restrict__ value_cache, int64_t total_vecs, int vecs_per_head, int heads,
-    int block_size, int64_t num_slots, int64_t key_stride_b, int64_t value_stride_b,
+    uint8_t *__restrict__ value_cache, uint32_t total_vecs, FastDiv per_token, FastDiv per_head,
+    FastDiv per_block, int64_t num_slots, int64_t key_stride_b, int64_t value_stride_b,
     int64_t block_stride_b, int64_t head_stride_b, int64_t entry_stride_b) {
-    const int64_t vecs_per_token = (int64_t)vecs_per_head * heads;
-    const int64_t step = (int64_t)gridDim.x * blockDim.x;
-    int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-
-    for (; i0 < total_vecs; i0 += step * UNROLL) {
+    const uint32_t step = gridDim.x * blockDim.x;
+    for (uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < total_vecs;
+         i0 += step * UNROLL) {
         uint4 kv[UNROLL], vv[UNROLL];
         int64_t dst[UNROLL];
 #pragma unroll
         for (int u = 0; u < UNROLL; ++u) {
-            const int64_t i = i0 + (int64_t)u * step;
+            const uint32_t i = i0 + (uint32_t)u * step;
             dst[u] = -1;
             if (i < total_vecs) {
-                const int64_t t = i / vecs_per_token;
-                const int r = (int)(i - t * vecs_per_token);
-                const int h = r / vecs_per_head;
-                const int c = r - h * vecs_per_head;
+                const uint32_t t = fdiv(i, per_token);
+                const uint32_t r = i - t * per_token.d;
+                const uint32_t h = fdiv(r, per_head);
+                const uint32_t c = r - h * per_head.d;
                 const int64_t slot = __ldg(slot_mapping + t);
                 // K/V loads independent of the slot: in flight with the slot load
-                kv[u] = ld_stream16(key + t * key_stride_b + (int64_t)r * 16);
-                vv[u] = ld_stream16(value + t * value_stride_b + (int64_t)r * 16);
+                kv[u] = ld_stream16(key + (int64_t)t * key_stride_b + (int64_t)r * 16);
+                vv[u] = ld_stream16(value + (int64_t)t * value_stride_b + (int64_t)r * 16);
                 if (slot >= 0 && slot < num_slots) {
-                    const int64_t blk = slot / block_size;
-                    const int64_t off = slot - blk * block_size;
-                    dst[u] = blk * block_stride_b + h * head_stride_b + off * entry_stride_b +
-                             (int64_t)c * 16;
+                    const uint32_t s32 = (uint32_t)slot;   // num_slots < 2^31 on this path
+                    const uint32_t blk = fdiv(s32, per_block);
+                    const uint32_t off = s32 - blk * per_block.d;
+                    dst[u] = (int64_t)blk * block_stride_b + (int64_t)h * head_stride_b +
+                             (int64_t)off * entry_stride_b + (int64_t)c * 16;
                 }
             }
         }
@@ -272,24 +291,42 @@ cudaError_t launch_reshape_and_cache(const ReshapeAndCacheArgs &a, int num_sms,
     const bool vec = (row_bytes % 16 == 0) && aligned16(a.key) && aligned16(a.value) &&
                      aligned16(a.key_cache) && aligned16(a.value_cache) &&
                      ((a.key_stride * eb) % 16 == 0) && ((a.value_stride * eb) % 16 == 0);
-    if (vec) {
+    const int64_t total_vec = vec ? (int64_t)a.num_tokens * a.num_kv_heads * (row_bytes / 16) : 0;
+    if (vec && total_vec < (1ll << 31) && num_slots < (1ll << 31)) {
         const int vecs_per_head = row_bytes / 16;
-        const int64_t total = (int64_t)a.num_tokens * a.num_kv_heads * vecs_per_head;
+        const uint32_t total = (uint32_t)total_vec;
         const int threads = 256;
-        const int64_t cap = (int64_t)num_sms * 8;   // 8 resident CTAs of 256 per SM
-        // one pass when everything fits in the resident CTAs: 2 vectors per thread
-        // (twice the CTAs) below half of that, 4 otherwise; larger T strides
-        const bool small = total <= cap * threads * 2;
+        // resident CTAs per SM of each instantiation (register-limited), looked up once
+        static int resident[2] = {0, 0};
+        if (resident[0] == 0) {
+            int r2 = 0, r4 = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r2, reshape_and_cache_vec16_kernel<2>,
+                                                          threads, 0);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r4, reshape_and_cache_vec16_kernel<4>,
+                                                          threads, 0);
+            resident[0] = r2 > 0 ? r2 : 4;
+            resident[1] = r4 > 0 ? r4 : 4;
+        }
+        // one pass with every load in flight when the launch fits the resident CTAs:
+        // 2 vectors per thread below half of that, 4 otherwise; larger T strides over
+        // exactly the resident grid
+        const int64_t cap2 = (int64_t)num_sms * resident[0];
+        const int64_t cap4 = (int64_t)num_sms * resident[1];
+        const bool small = total <= cap2 * threads * 2;
         const int unroll = small ? 2 : 4;
-        const int64_t want = (total + (int64_t)threads * unroll - 1) / ((int64_t)threads * unroll);
+        const int64_t cap = small ? cap2 : cap4;
+        const int64_t want = ((int64_t)total + (int64_t)threads * unroll - 1) /
+                             ((int64_t)threads * unroll);
         const int64_t grid = want < 1 ? 1 : (want < cap ? want : cap);
         auto kfn = small ? reshape_and_cache_vec16_kernel<2> : reshape_and_cache_vec16_kernel<4>;
         kfn<<<(unsigned)grid, threads, 0, stream>>>(
             static_cast<const uint8_t *>(a.key), static_cast<const uint8_t *>(a.value),
             a.slot_mapping, static_cast<uint8_t *>(a.key_cache),
-            static_cast<uint8_t *>(a.value_cache), total, vecs_per_head, a.num_kv_heads,
-            a.block_size, num_slots, a.key_stride * eb, a.value_stride * eb,
-            a.block_stride * eb, a.head_stride * eb, a.entry_stride * eb);
+            static_cast<uint8_t *>(a.value_cache), total,
+            make_fastdiv((uint32_t)(vecs_per_head * a.num_kv_heads)),
+            make_fastdiv((uint32_t)vecs_per_head), make_fastdiv((uint32_t)a.block_size),
+            num_slots, a.key_stride * eb, a.value_stride * eb, a.block_stride * eb,
+            a.head_stride * eb, a.entry_stride * eb);
     } else {
         const int64_t total = (int64_t)a.num_tokens * a.num_kv_heads * a.size_per_head;
         int64_t grid = (total + 255) / 256;

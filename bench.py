@@ -886,7 +886,7 @@ def run_extras(args, peaks, torch):
     W = Llama8B()
     tr, tp = timed_loop(torch, args.steps, args.warmup, [W.reshape, W.prefill], flush=W.flush)
     k_ms = trimmed_mean(tp)
-    traffic = load_traffic().get("fa_prefill_tcgen05_sm100/config2")
+    traffic = load_traffic().get("fa_prefill_tcgen05_sm100/llama8b")
     ex["llama8b_prefill"] = {
         "workload": "Llama-3-8B varlen causal prefill, 4 seqs L~U{512..2048} "
                     f"({'+'.join(map(str, W.lens))} tokens), Hq 32, Hkv 8, D 128, bs 16, bf16; "
@@ -1110,6 +1110,9 @@ def run_only(args, dd, torch):
         if args.only == "decode8b_fp8":
             W.setup_decode_fp8()
             ph = [W.decode_reshape_fp8, W.decode_fp8]
+    elif args.only == "rms_norm":
+        print(json.dumps({"only": "rms_norm", **run_rms(args, load_peaks()[0], torch)}))
+        return
     elif args.only.startswith("reshape"):
         R = ReshapeSweep()
         T = int(args.only[len("reshape"):] or 65536)
@@ -1135,7 +1138,7 @@ def main():
                     help="analysis: time rank 0's shard of an N-way KV-head split on one GPU")
     ap.add_argument("--only", default=None,
                     help="one workload's timed loop (prefill70b, decode70b, prefill8b, "
-                         "prefill8b_fp8, decode8b, decode8b_fp8, reshape<T>)")
+                         "prefill8b_fp8, decode8b, decode8b_fp8, rms_norm, reshape<T>)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

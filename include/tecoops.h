@@ -323,6 +323,8 @@ tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(tecoopsHandle_t handle, int m
  * kernel reported an error since the previous call (and clears it),
  * TECOOPS_STATUS_SUCCESS otherwise; *error_code receives the first code found:
  *   0x1nn-0xann  tcgen05 prefill: a bounded wait gave up (site in the high byte)
+ *   0xb00        tcgen05 prefill: a q_seq_lens entry exceeds max_seqlen_q (rows past
+ *                the planned work units were not computed)
  *   0x11nn       split-KV decode: the producer's wait for a free ring stage gave up
  *   0x12nn       split-KV decode: a consumer's wait for a loaded chunk gave up
  *   0x1300       split-KV decode: a kv_seq_lens entry exceeds max_seqlen_k (the keys

@@ -131,6 +131,9 @@ enum WaitSite : int {
     kSiteQ = 0x100, kSiteK = 0x200, kSiteV = 0x300, kSiteEmpty = 0x400, kSiteS = 0x500,
     kSiteP = 0x600, kSiteO = 0x700, kSiteDrain = 0x800, kSiteVz = 0x900, kSiteSched = 0xa00
 };
+// caller error the scheduler detects: a q_seq_lens entry above max_seqlen_q (the work
+// units are planned from max_seqlen_q; rows past the plan are not computed)
+constexpr int kErrQBeyondPlan = 0xb00;
 
 // barrier slots
 constexpr int Q_FULL = 0, K_FULL = 1, K_EMPTY = 4, V_FULL = 7, V_EMPTY = 9, S_FULL = 11,
@@ -329,6 +332,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int b = (c / HP) % p.batch;
                     const int L = __ldg(p.q_seq_lens + b);
                     const int unit = p.num_units - 1 - c / (HP * p.batch);
+                    if (unit == p.num_units - 1 && lane == 0 &&
+                        L > p.num_units * (p.pair_heads ? kBM : 2 * kBM))
+                        atomicCAS(p.dev_error, 0, kErrQBeyondPlan);
                     if (unit * (p.pair_heads ? kBM : 2 * kBM) < L) {
                         e = make_int4(c, L, __ldg(p.kv_seq_lens + b),
                                       warp_seq_start(p.q_seq_lens, b));

@@ -137,3 +137,27 @@ def test_q_len_above_one_on_the_decode_path_is_reported():
         assert st == capi.INTERNAL_ERROR and code == Q_LEN_ABOVE_ONE, hex(code)
     finally:
         h.close()
+
+
+def test_q_len_above_max_seqlen_q_on_the_prefill_path_is_reported():
+    """The prefill's work units are planned from max_seqlen_q: a sequence longer than that
+    has rows past the plan, which are not computed; the scheduler reports it (0xb00)."""
+    from gpu_util import attention_capi
+    from tecoops import capi
+    L, Hq, Hkv, D, bs = 300, 8, 2, 128, 16
+    g = torch.Generator(device="cuda").manual_seed(72)
+    q = torch.randn(L, Hq, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    pages = (L + bs - 1) // bs
+    kc = torch.randn(pages, Hkv, bs, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    vc = torch.randn_like(kc)
+    bt = torch.arange(pages, dtype=torch.int32, device="cuda")[None]
+    lens = torch.tensor([L], dtype=torch.int32, device="cuda")
+    h = capi.Handle(torch.cuda.current_stream().cuda_stream)
+    try:
+        attention_capi(q, kc, vc, lens, lens, bt, max_q=200, max_k=L, h=h)   # plans 256 rows
+        st, code = capi.device_error(h)
+        assert st == capi.INTERNAL_ERROR and code == 0xb00, hex(code)
+        attention_capi(q, kc, vc, lens, lens, bt, max_q=L, max_k=L, h=h)
+        assert capi.device_error(h) == (capi.SUCCESS, 0)
+    finally:
+        h.close()

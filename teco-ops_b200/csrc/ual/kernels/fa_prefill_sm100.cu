@@ -647,7 +647,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < kBN / 32; ++c) {
                     uint32_t pk[16];
-                    if (masked)
+                    // a chunk masked for every row of the warp (the upper triangle of the
+                    // diagonal tile, keys past kv_len, keys before a window) needs no exp2
+                    if (masked && __all_sync(0xffffffffu, nvalid - c * 32 <= 0 ||
+                                                              nlo - c * 32 >= 32)) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) pk[e] = 0u;
+                    } else if (masked)
                         chunk_exp<T, true>(uu[c], nlo - c * 32, nvalid - c * 32, sl2x2, negm2,
                                            sum2, pk);
                     else

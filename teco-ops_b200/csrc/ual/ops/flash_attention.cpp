@@ -149,8 +149,15 @@ static cudaError_t runGeneric(const FlashAttentionArgs &a, cudaStream_t stream) 
     return kern::launch_generic_attention(toShape(a), a.dtype == ElemType::BF16, stream);
 }
 
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 FlashAttentionAlgos FlashAttentionOp::selectAlgo(const FlashAttentionArgs &a) {
     const int group = a.local_head_num / a.local_kv_head_num;
+    // the tuned kernels move q, out and the caches in 16-byte vectors, TMA boxes and TMA
+    // stores; a view that is only element-aligned takes the generic kernel (scalar access)
+    if (!aligned16(a.q) || !aligned16(a.fmha_out) || !aligned16(a.key_cache) ||
+        !aligned16(a.value_cache) || !aligned16(a.new_key) || !aligned16(a.new_value))
+        return FlashAttentionAlgos::GENERIC;
     if (a.max_q_seq_len == 1 && kern::decode_supported(a.size_per_head, a.block_size, group))
         return FlashAttentionAlgos::DECODE_SPLITKV;
     // e4m3 caches reach the tcgen05 prefill through a dequantised compact copy

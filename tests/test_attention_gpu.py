@@ -250,3 +250,37 @@ def test_config5_decode_sampled_sequences():
                                        np.arange(pages[b], dtype=np.int32)[None])
         mx, mean, diff1 = errors(out[b:b + 1].float().cpu().numpy(), ref)
         assert mx <= MAX_ABS and mean <= MEAN_ABS and diff1 <= DIFF1, (b, mx, mean, diff1)
+
+
+@pytest.mark.parametrize("name", ["bf16_bs16_varlen", "bf16_bs16_decode"])
+@pytest.mark.parametrize("offset_elems", [0, 8, 16, 1])
+def test_output_alignment_paths(name, offset_elems):
+    """The prefill epilogue writes whole 32-row warp tiles by TMA store when `out` is
+    16-byte aligned and falls back to row stores otherwise (and for partial warp tiles);
+    a q or out that is only element-aligned (a view at an odd element offset) takes the
+    generic kernel, whose accesses are scalar.  Every alignment must match the aligned
+    call (bit-exactly where the same kernel runs, within the attention tolerance on the
+    generic kernel), and nothing outside `out` may change.  Offsets in elements: 8 = 16
+    bytes (TMA stores, 16-byte row stores), 16 = 32 bytes, 1 = 2 bytes (generic)."""
+    from gpu_util import attention_capi, attn_case_to_dev
+    c = cases.ATTN_CASES[name]
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    max_q = 1 if "decode" in name else None
+    ref = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"],
+                         max_q=max_q)
+    n = d["q"].numel()
+    buf = torch.full((n + offset_elems + 64,), 7.0, device="cuda", dtype=d["q"].dtype)
+    out = buf[offset_elems:offset_elems + n].view(d["q"].shape)
+    qbuf = torch.empty(n + offset_elems, device="cuda", dtype=d["q"].dtype)
+    q = qbuf[offset_elems:].view(d["q"].shape)
+    q.copy_(d["q"])
+    got = attention_capi(q, d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"], out=out,
+                         max_q=max_q)
+    torch.cuda.synchronize()
+    if offset_elems % 8 == 0:
+        assert torch.equal(got, ref)
+    else:
+        diff = (got.float() - ref.float()).abs()
+        assert diff.max().item() <= MAX_ABS and diff.mean().item() <= MEAN_ABS
+    assert (buf[:offset_elems] == 7.0).all() and (buf[offset_elems + n:] == 7.0).all()

@@ -228,6 +228,18 @@ extern "C" tecoopsStatus_t tecoopsReshapeAndCacheFlashAttentionDecode(
     if (!qData || !oData) return TECOOPS_STATUS_BAD_PARAM;
     FlashAttentionArgs args{};
     fillArgs(args, handle, 1, max_seqlen_k, blockTableDesc, qDataDesc, kCacheDesc);
+    // every pointer before the branch choice: it depends on their alignment, and only the
+    // split-KV kernel performs the scatter of the new tokens itself
+    args.q_seq_lens = q_seq_lens;
+    args.kv_seq_lens = kv_seq_lens;
+    args.block_table = static_cast<const int *>(blockTable);
+    args.q = qData;
+    args.key_cache = kCache;
+    args.value_cache = vCache;
+    args.fmha_out = oData;
+    args.new_key = key;
+    args.new_value = value;
+    args.slot_mapping = slot_mapping;
     if (FlashAttentionOp::selectAlgo(args) !=
             tecoops::ual::ops::FlashAttentionAlgos::DECODE_SPLITKV ||
         (args.size_per_head % 8) != 0) {
@@ -241,16 +253,6 @@ extern "C" tecoopsStatus_t tecoopsReshapeAndCacheFlashAttentionDecode(
                                   kCache, vCacheDesc, vCache, oDataDesc, oData, workspace,
                                   nullptr, nullptr);
     }
-    args.q_seq_lens = q_seq_lens;
-    args.kv_seq_lens = kv_seq_lens;
-    args.block_table = static_cast<const int *>(blockTable);
-    args.q = qData;
-    args.key_cache = kCache;
-    args.value_cache = vCache;
-    args.fmha_out = oData;
-    args.new_key = key;
-    args.new_value = value;
-    args.slot_mapping = slot_mapping;
     const size_t need = FlashAttentionOp::workspaceSize(args);
     if (workspace != nullptr) {
         args.workspace = workspace;

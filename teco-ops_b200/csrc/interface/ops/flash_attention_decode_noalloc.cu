@@ -132,6 +132,14 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
         return TECOOPS_STATUS_BAD_PARAM;
     if (!packedDesc(q) || !packedDesc(o) || !packedDesc(k) || !packedDesc(v) || !packedDesc(bt))
         return TECOOPS_STATUS_NOT_SUPPORTED;
+    // the split-KV kernel reads q in 32-bit words and the caches by TMA (16-byte aligned)
+    const uintptr_t al = reinterpret_cast<uintptr_t>(qData) | reinterpret_cast<uintptr_t>(oData) |
+                         reinterpret_cast<uintptr_t>(kCache) | reinterpret_cast<uintptr_t>(vCache);
+    if (al & 15u) {
+        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: q, out and the caches must be 16-byte "
+                   "aligned");
+        return TECOOPS_STATUS_NOT_SUPPORTED;
+    }
     const int batch = bt->dimA[0], heads = q->dimA[1], kv_heads = k->dimA[1];
     const int head_dim = q->dimA[2], block_size = k->dimA[2];
     const int group = heads / kv_heads;

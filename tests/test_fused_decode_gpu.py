@@ -18,7 +18,7 @@ def _need_cuda():
         pytest.skip("no CUDA device")
 
 
-def _run(c, pad_first=False, seed=7):
+def _run(c, pad_first=False, seed=7, kv_offset=0):
     from gpu_util import TORCH_DT, attention_capi, attn_case_to_dev, handle, reshape_capi
     from tecoops import capi
     inp = cases.attn_inputs(c)
@@ -28,6 +28,13 @@ def _run(c, pad_first=False, seed=7):
     g = torch.Generator(device="cuda").manual_seed(seed)
     knew = torch.randn(B, Hkv, D, device="cuda", generator=g).to(TORCH_DT[c["dtype"]])
     vnew = torch.randn(B, Hkv, D, device="cuda", generator=g).to(TORCH_DT[c["dtype"]])
+    if kv_offset:   # the same values in views that start kv_offset elements into a buffer
+        kb = torch.empty(knew.numel() + kv_offset, device="cuda", dtype=knew.dtype)
+        vb = torch.empty_like(kb)
+        kb[kv_offset:].copy_(knew.flatten())
+        vb[kv_offset:].copy_(vnew.flatten())
+        knew = kb[kv_offset:].view(knew.shape)
+        vnew = vb[kv_offset:].view(vnew.shape)
     kl = inp["kv_lens"]
     slot = [int(inp["block_table"][b, (int(kl[b]) - 1) // bs]) * bs + (int(kl[b]) - 1) % bs
             for b in range(B)]
@@ -67,6 +74,15 @@ def test_fused_decode_matches_two_operators(name):
                                    inp["block_table"])
     mx, mean, _ = errors(out_b.float().cpu().numpy(), ref)
     assert mx <= 2e-2 and mean <= 2e-3, (mx, mean)
+
+
+def test_fused_decode_element_aligned_new_kv():
+    """New K/V views at an odd element offset cannot feed the kernel's 16-byte scatter:
+    the call runs the two operators instead, with the same results."""
+    c = cases.ATTN_CASES["bf16_bs16_decode"]
+    inp, d, (kc_a, vc_a, out_a), (kc_b, vc_b, out_b) = _run(c, kv_offset=1)
+    assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
+    assert torch.equal(out_a, out_b)
 
 
 def test_fused_decode_padding_slot_leaves_cache():

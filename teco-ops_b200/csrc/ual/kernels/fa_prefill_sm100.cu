@@ -118,6 +118,7 @@ struct PrefillParams {
     float *lse;         // optional [Hq, total_q] natural-log log-sum-exp
     int out_al32;       // out is 32-byte aligned: rows are written with 256-bit stores
     int out_tma;        // out is 16-byte aligned: full 32-row warp tiles leave by TMA store
+    int late_draw;      // draw each CTA's next unit late (few units per CTA)
 };
 
 // eight 32-bit words to a 32-byte aligned global address in one instruction
@@ -347,16 +348,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) {
                     sched_slot[k & 3] = e;
                     mbar_arrive(BAR(SCHED_FULL + (k & 3)));
-                    // the next draw is in flight while this unit's tiles are issued
-                    if (e.x >= 0) next = (int)gridDim.x + atomicAdd(p.sched, 1);
+                    // many units per CTA: the next draw is in flight while this unit's
+                    // tiles are issued (see draw_next for the few-units case)
+                    if (e.x >= 0 && !p.late_draw) next = (int)gridDim.x + atomicAdd(p.sched, 1);
                 }
                 next = __shfl_sync(0xffffffffu, next, 0);
             } else {
                 e = take_unit_warp(k);
             }
             if (e.x < 0) break;
+            // few units per CTA (p.late_draw): the next unit is drawn once this unit's last
+            // K tile is issued (about two tiles before it ends), so the choice follows the
+            // CTAs' actual progress -- longest-first list scheduling, which evens out the
+            // end of the kernel; with many units per CTA the early draw measured faster
+            bool drawn = !p.late_draw;
+            auto draw_next = [&]() {
+                if (!isV && !drawn) {
+                    if (lane == 0) next = (int)gridDim.x + atomicAdd(p.sched, 1);
+                    next = __shfl_sync(0xffffffffu, next, 0);
+                    drawn = true;
+                }
+            };
             Unit u;
-            if (!decode_unit(e, u) || u.N == 0) continue;
+            if (!decode_unit(e, u) || u.N == 0) {
+                draw_next();
+                continue;
+            }
             const int qs = u.qs;
             if (!isV && lane == 0) {
                 // Q buffers are free once the previous unit's last S MMAs completed
@@ -414,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     row, u.kvh, blk);
                 }
             }
+            draw_next();
             // V rows of the unit's last tile past kv_len may hold arbitrary bits
             // (unwritten cache slots): clear them before the PV MMAs of that tile
             if (ok && isV && u.N * kBN > u.S) {
@@ -872,6 +890,7 @@ static cudaError_t launch_prefill_t(const AttnShape &s, int *dev_error, int num_
         p.num_units * s.batch * (p.pair_heads ? s.num_heads / 2 : s.num_heads);
     // persistent: one CTA per SM, units handed out by the in-kernel scheduler
     dim3 grid(units_total < num_sms ? units_total : num_sms);
+    p.late_draw = units_total < 12 * (int)grid.x ? 1 : 0;   // fewer than ~12 per CTA
     kfn<<<grid, kThreads, smem, stream>>>(qmap, kmap, vmap, omap, p);
     return cudaGetLastError();
 }

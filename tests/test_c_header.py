@@ -37,3 +37,31 @@ def test_c99_client_compiles_links_and_runs(tmp_path, cuda_first):
     r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "c99 client OK" in r.stdout
+
+
+def _build_decode_step(tmp_path):
+    exe = str(tmp_path / "decode_step")
+    cmd = ["gcc", "-std=c99", "-Wall", "-Werror", "-O1", "-I" + os.path.join(ROOT, "include"),
+           "-I/usr/local/cuda/include", os.path.join(ROOT, "tests", "c_api", "decode_step.c"),
+           "-o", exe, "-L" + LIBDIR, "-lteco_ops", "-L/usr/local/cuda/lib64", "-lcudart", "-lm",
+           "-Wl,-rpath," + LIBDIR, "-Wl,-rpath,/usr/local/cuda/lib64"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return exe
+
+
+def test_c99_gpu_client_compiles(tmp_path):
+    """The GPU decode-step client below compiles and links as C99 (no GPU needed)."""
+    if not os.path.exists(os.path.join(LIBDIR, "libteco_ops.so")):
+        pytest.skip("libteco_ops.so not built")
+    _build_decode_step(tmp_path)
+
+
+@pytest.mark.gpu
+def test_c99_gpu_client_runs_a_decode_step(tmp_path):
+    """tests/c_api/decode_step.c: reshape_and_cache + flash_attention from plain C on the
+    GPU, checked on the host against an fp32 loop within the attention tolerances."""
+    exe = _build_decode_step(tmp_path)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "c99 gpu client OK" in r.stdout

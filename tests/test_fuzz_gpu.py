@@ -1,0 +1,101 @@
+"""Seeded random sweep of the attention entry point against the CPU oracle.
+
+The hand-picked parity cases follow the reference's tests; this sweep adds shapes
+nobody picked: 1-6 sequences, query lengths 0..300 with kv lengths >= them (chunked
+prefill, empty sequences, kv lengths that end anywhere in a page or tile), GQA groups 1,
+2, 3, 4, 8, head_dim 64 / 128, block sizes 8..256, fp16 / bf16, shuffled page pools
+with spare pages, and decode calls (every q_len 0 or 1) through the split-KV branch.
+Every case must meet the north-star tolerance (max-abs <= 2e-2, mean-abs <= 2e-3)."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from oracle import seeded
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(i):
+    rng = np.random.default_rng(9000 + i)
+    decode = i % 4 == 3
+    B = int(rng.integers(1, 7))
+    Hkv = int(rng.choice([1, 2, 4]))
+    group = int(rng.choice([1, 2, 3, 4, 8]))
+    D = int(rng.choice([64, 128]))
+    bs = int(rng.choice([8, 16, 32, 64, 128, 256]))
+    kv = [int(rng.integers(1, 600)) for _ in range(B)]
+    if decode:
+        q = [int(rng.integers(0, 2)) for _ in range(B)]
+        q[0] = 1
+    else:
+        q = [int(min(k, rng.integers(0, 301))) for k in kv]
+        q[0] = max(q[0], 1)
+    pages = sum((k + bs - 1) // bs for k in kv)
+    return cases._fa(q, kv, Hkv * group, Hkv, D, bs, pages + int(rng.integers(0, 9)),
+                     str(rng.choice(["f16", "bf16"])), "normal", 500 + i, golden=False)
+
+
+@pytest.mark.parametrize("i", range(40))
+def test_random_shapes_match_the_oracle(i):
+    from gpu_util import attention_capi, attn_case_to_dev, errors
+    c = _case(i)
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    out = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"],
+                         out=torch.full_like(d["q"], 3.0))
+    torch.cuda.synchronize()
+    ref = oracle.flash_attn_varlen(
+        seeded.words_to_f32(inp["q"], c["dtype"]), seeded.words_to_f32(inp["k_cache"], c["dtype"]),
+        seeded.words_to_f32(inp["v_cache"], c["dtype"]), inp["q_lens"], inp["kv_lens"],
+        inp["block_table"])
+    got = out.float().cpu().numpy()
+    mx, mean, _ = errors(got, ref)
+    assert mx <= 2e-2 and mean <= 2e-3, (c, mx, mean)
+
+
+LSE_ABS = 2e-3   # log-sum-exp (natural log), as in the hand-picked options cases
+
+
+def _opts(rng):
+    o = {"lse": True}
+    if rng.random() < 0.3:
+        o["causal"] = False
+    if rng.random() < 0.4:
+        o["scale"] = float(rng.uniform(0.02, 0.4))
+    if rng.random() < 0.6:
+        left = int(rng.choice([-1, 0, int(rng.integers(1, 400))]))
+        right = int(rng.choice([-1, 0, int(rng.integers(1, 200))]))
+        o["window"] = (left, right)
+    return o
+
+
+@pytest.mark.parametrize("i", range(24))
+def test_random_options_match_the_oracle(i):
+    """tecoopsFlashAttentionEx (causal or not, sliding windows, custom scale, the
+    log-sum-exp output) on random shapes of the sweep above.  Rows whose window admits
+    no key have output 0 and log-sum-exp -inf in both."""
+    from gpu_util import attention_ex_capi, attn_case_to_dev, errors
+    c = _case(100 + i)
+    opts = _opts(np.random.default_rng(7000 + i))
+    c["opts"] = opts
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    out, lse = attention_ex_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"],
+                                 opts)
+    torch.cuda.synchronize()
+    ref, rlse = oracle.flash_attn_varlen(
+        seeded.words_to_f32(inp["q"], c["dtype"]), seeded.words_to_f32(inp["k_cache"], c["dtype"]),
+        seeded.words_to_f32(inp["v_cache"], c["dtype"]), inp["q_lens"], inp["kv_lens"],
+        inp["block_table"], return_lse=True, **cases.attn_opts(c))
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all(), c
+    mx, mean, _ = errors(got, ref)
+    assert mx <= 2e-2 and mean <= 2e-3, (c, mx, mean)
+    lse = lse.cpu().numpy()
+    fin = np.isfinite(rlse)
+    assert np.array_equal(np.isfinite(lse), fin) and not np.isnan(lse).any(), c
+    if fin.any():
+        err = np.abs(lse[fin] - rlse[fin]).max()
+        assert err <= LSE_ABS, (c, err)

@@ -440,6 +440,23 @@ class Llama70B:
         return res
 
 
+def gpu_local_cpus(torch):
+    """CPUs next to the current GPU (NVML's CPU affinity of the device, within this
+    process's allowed set), or None when NVML cannot say."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        n = os.cpu_count() or 1
+        mask = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
+        cpus = {64 * w + b for w, m in enumerate(mask) for b in range(64) if (m >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:   # no NVML, or no affinity information on this host
+        return None
+
+
 def run_e2e_prefill(W, args, dd):
     """The headline prefill step through the public torch API (tecoops.reshape_and_cache
     + tecoops.flash_attn_varlen_func) with this rank's inputs in pinned host memory:
@@ -451,6 +468,23 @@ def run_e2e_prefill(W, args, dd):
     upload to the last download, max over ranks."""
     import tecoops
     torch = W.torch
+    # the pinned buffers' pages go to the NUMA node of the CPUs that first touch them:
+    # run this rank on the CPUs next to its GPU while they are made and used, so that the
+    # copies do not cross the socket link (the previous affinity is restored afterwards)
+    old_cpus = os.sched_getaffinity(0)
+    near = gpu_local_cpus(torch)
+    if near:
+        os.sched_setaffinity(0, near)
+    try:
+        res = _e2e_prefill_loop(W, args, dd, tecoops, torch)
+    finally:
+        os.sched_setaffinity(0, old_cpus)
+    res["host_cpus"] = (f"{len(near)} CPUs next to the GPU (NVML affinity)" if near
+                        else "unbound (no NVML CPU affinity)")
+    return res
+
+
+def _e2e_prefill_loop(W, args, dd, tecoops, torch):
     host = {n: t.cpu().pin_memory() for n, t in
             (("q", W.q), ("k", W.k), ("v", W.v), ("slot", W.slot), ("bt", W.bt))}
     cu = torch.zeros(len(W.lens) + 1, dtype=torch.int32)

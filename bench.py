@@ -802,10 +802,169 @@ def cfg1_pair(torch, capi, steps, warmup):
             "prefill_step_us": step_ms(tp) * 1e3,
             "prefill_kernel_us": trimmed_mean(tp[1]) * 1e3,
             "prefill_tflops": fl / (trimmed_mean(tp[1]) * 1e-3) / 1e12,
-            "l2": "flushed between steps (inputs < L2); latency-bound at this size"}
+            "l2": "flushed between steps (inputs < L2); latency-bound at this size",
+            "cpu_baseline": cpu_pair(torch, key, val, slot, pslot, q, bt, out, NB, n_valid)}
+
+
+def cpu_pair(torch, key, val, slot, pslot, q, bt, out_gpu, NB, n_valid):
+    """The fp16 pair on the host (same inputs): reshape_and_cache of the 256 tokens (C
+    restatement, one thread) and the step of reshape (prefill slots) + the reference
+    golden prefill (torch fp32, all host threads); medians of 3 after a warm-up."""
+    import numpy as np
+
+    import oracle
+    golden = _golden_or_none()
+    kw, vw = _words(key), _words(val)
+    sl, psl = slot.cpu().numpy(), pslot.cpu().numpy()
+    T, H = key.shape[0], key.shape[1]
+    kc = np.zeros((NB, H, BS, D), dtype=np.uint16)
+    vc = np.zeros_like(kc)
+    r_s = _median_s(lambda: oracle.reshape_and_cache(kw, vw, sl, kc, vc))
+    res = {"reshape_gbs": reshape_bytes(n_valid, T, hkv=H) / r_s / 1e9, "reshape_cores": 1,
+           "kind": "reference"}
+    if golden is None:
+        return res
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    qf, btc = q.cpu().float(), bt.cpu()
+    keep = {}
+
+    def step():
+        kc2 = np.zeros((NB, H, BS, D), dtype=np.uint16)
+        vc2 = np.zeros_like(kc2)
+        oracle.reshape_and_cache(kw, vw, psl, kc2, vc2)
+        keep["out"] = golden(qf, _cache_f32(torch, kc2, torch.float16),
+                             _cache_f32(torch, vc2, torch.float16), [T], [T], btc)
+    p_s = _median_s(step)
+    diff = (keep["out"] - out_gpu.cpu().float()).abs()
+    res.update({"prefill_step_tflops": attn_flops([T], [T], hq=H) / p_s / 1e12, "cores": threads,
+                "sample": f"in full: reshape {r_s * 1e6:.0f} us, reshape + golden prefill "
+                          f"{p_s * 1e3:.2f} ms (medians of 3)",
+                "gpu_vs_golden": {"max_abs": float(diff.max()), "mean_abs": float(diff.mean())}})
+    return res
 
 
 # ----------------------------------------------------------------------------- CPU arm
+def _median_s(fn, runs=3, warmup=1):
+    """Wall-clock median of `runs` calls of fn after `warmup` calls."""
+    for _ in range(warmup):
+        fn()
+    ts = []
+    for _ in range(runs):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return sorted(ts)[len(ts) // 2]
+
+
+def _words(t):
+    """A CUDA or CPU 16-bit tensor as a host numpy array of uint16 words."""
+    import numpy as np
+    return t.contiguous().cpu().view(__import__("torch").int16).numpy().view(np.uint16)
+
+
+def _cache_f32(torch, words, dtype):
+    """The golden's input conversion (python_api_test/test_flash_attention.py:167-181):
+    16-bit cache words [NB, H, bs, D] -> fp32 [NB, bs, H, D]."""
+    return (torch.from_numpy(words.view("int16")).view(dtype).float().permute(0, 2, 1, 3)
+            .contiguous())
+
+
+def _cpu_result(value, unit, sample, threads, extra=None):
+    r = {"value": value, "unit": unit, "cores": threads, "kind": "reference", "sample": sample}
+    if extra:
+        r.update(extra)
+    return r
+
+
+def cpu_llama8b_prefill(W, golden):
+    """The whole Llama-3-8B prefill step on the host cores: reshape_and_cache of all tokens
+    (C restatement of the reference loop, one thread) and the reference golden over the
+    batch (torch fp32, all host threads); median of 3 after a warm-up.  Also compares the
+    GPU output of the same inputs with the golden's."""
+    import numpy as np
+    import torch
+
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    kw, vw, slot = _words(W.k), _words(W.v), W.slot.cpu().numpy()
+    q = W.q.cpu().float()
+    bt = W.bt.cpu()
+    res = {}
+
+    def step():
+        kc = np.zeros((W.nb, W.HKV, BS, D), dtype=np.uint16)
+        vc = np.zeros_like(kc)
+        oracle.reshape_and_cache(kw, vw, slot, kc, vc)
+        res["out"] = golden(q, _cache_f32(torch, kc, torch.bfloat16),
+                            _cache_f32(torch, vc, torch.bfloat16), W.lens, W.lens, bt)
+    secs = _median_s(step)
+    diff = (res["out"] - W.out.cpu().float()).abs()
+    return _cpu_result(W.flops / secs / 1e12, "TFLOP/s",
+                       f"the whole step (reshape_and_cache of {W.tot} tokens + the golden "
+                       f"flash_attn_varlen_func over the {len(W.lens)} sequences), median of 3: "
+                       f"{secs:.2f} s",
+                       threads, {"gpu_vs_golden": {"max_abs": float(diff.max()),
+                                                   "mean_abs": float(diff.mean())}})
+
+
+def cpu_llama8b_decode(W, golden, out_gpu):
+    """The Llama-3-8B decode step on the host cores: reshape_and_cache of the 64 new tokens
+    (C loop) and the golden for every sequence on its own pages (the cache compacted per
+    sequence, block table remapped to 0..n-1: the golden's math unchanged, its fp32
+    conversion limited to the pages the sequence reads); median of 3."""
+    import numpy as np
+    import torch
+
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    kc, vc = _words(W.d_kc), _words(W.d_vc)     # the pool (2 x 1.3 GB), copied untimed
+    kw, vw, slot = _words(W.d_knew), _words(W.d_vnew), W.d_slot.cpu().numpy()
+    q = W.d_q3.cpu().float()
+    ctx = W.d_ctx.cpu().tolist()
+    bt = W.d_bt3.cpu().numpy()
+    outs = [None] * W.d_B
+
+    def step():
+        oracle.reshape_and_cache(kw, vw, slot, kc, vc)
+        for b in range(W.d_B):
+            pages = bt[b, :cdiv(ctx[b], BS)]
+            outs[b] = golden(q[b:b + 1], _cache_f32(torch, kc[pages], torch.bfloat16),
+                             _cache_f32(torch, vc[pages], torch.bfloat16), [1], [ctx[b]],
+                             torch.arange(len(pages), dtype=torch.int32)[None])
+    secs = _median_s(step, runs=3, warmup=0)
+    diff = (torch.cat(outs) - out_gpu.cpu().float()).abs()
+    step_bytes = W.decode_bytes + W.decode_reshape_bytes
+    return _cpu_result(step_bytes / secs / 1e9, "GB/s",
+                       f"the whole step (reshape_and_cache of {W.d_B} tokens + the golden per "
+                       f"sequence on its compacted pages), median of 3: {secs:.2f} s", threads,
+                       {"gpu_vs_golden": {"max_abs": float(diff.max()),
+                                          "mean_abs": float(diff.mean())}})
+
+
+def cpu_reshape_sweep(R, points):
+    """Every point of the reshape sweep on the host: the C restatement of the reference
+    loop, one thread as the reference runs it, into host caches of the same 65,536 pages
+    (touched before timing); median of 3 (2 at T = 65,536)."""
+    import numpy as np
+    kw, vw = _words(R.k), _words(R.v)
+    kc = np.ones((R.NB, R.HKV, BS, D), dtype=np.uint16)
+    vc = np.ones_like(kc)
+    import oracle
+    for pt in points:
+        T = pt["T"]
+        slot, nv = R.slots(T, pt["slots"] == "scattered", pt["pad"])
+        sl = slot.cpu().numpy()
+        secs = _median_s(lambda: oracle.reshape_and_cache(kw[:T], vw[:T], sl, kc, vc),
+                         runs=2 if T >= 65536 else 3)
+        pt["cpu_gbs"] = pt["bytes"] / secs / 1e9
+    return {"unit": "GB/s", "cores": 1, "kind": "reference",
+            "sample": "every point in full (the C restatement of reshape_and_cache.cpp:136-147, "
+                      "one thread), median of 3 (2 at T = 65,536): cpu_gbs of each point"}
+
+
 def _ref_golden():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import install_ref
@@ -844,6 +1003,13 @@ def cpu_sample_70b(golden, b_idx, kv_head, rows=2048, threads=None):
     vf = torch.from_numpy(vc.view(np.int16)).view(torch.bfloat16).float().permute(0, 2, 1, 3)
     golden(q.float(), kf.contiguous(), vf.contiguous(), [rows], [L], bt)
     return attn_flops([rows], [L], hq=g), time.perf_counter() - t0
+
+
+def _golden_or_none():
+    try:
+        return _ref_golden()
+    except ImportError:
+        return None
 
 
 def cpu_baseline_70b(budget_s=15.0):
@@ -936,6 +1102,9 @@ def run_extras(args, peaks, torch):
                      "kernel_us": k_ms * 1e3, "flops_per_launch": W.flops,
                      "traffic": traffic, "peak_source": "bf16_tflops (burst)"},
         "l2": "flushed between timed steps (256 MB write)"}
+    golden = _golden_or_none()
+    if golden is not None:
+        ex["llama8b_prefill"]["cpu_baseline"] = cpu_llama8b_prefill(W, golden)
     W.setup_fp8()
     fr, fp = timed_loop(torch, args.steps, args.warmup, [W.reshape_fp8, W.prefill_fp8],
                         flush=W.flush)
@@ -945,6 +1114,7 @@ def run_extras(args, peaks, torch):
         "prefill_us": trimmed_mean(fp) * 1e3}
     W.setup_decode()
     tr, ta = timed_loop(torch, args.steps, args.warmup, [W.decode_reshape, W.decode])
+    out_bf16 = W.d_out3.clone()
     (tf,) = timed_loop(torch, args.steps, args.warmup, [W.decode_fused])
     W.setup_decode_fp8()
     fr, fa = timed_loop(torch, args.steps, args.warmup, [W.decode_reshape_fp8, W.decode_fp8])
@@ -967,6 +1137,8 @@ def run_extras(args, peaks, torch):
                       / peaks["hbm_gbs"],
                       "speedup_vs_bf16_step": s_ms / step_ms([fr, fa])},
         "l2": "inputs (1.1 GB of K/V) larger than L2"}
+    if golden is not None:
+        ex["llama8b_decode"]["cpu_baseline"] = cpu_llama8b_decode(W, golden, out_bf16)
     del W
     torch.cuda.empty_cache()
     R = ReshapeSweep()
@@ -986,6 +1158,7 @@ def run_extras(args, peaks, torch):
                     "per cache); bytes 8*T + 4*valid*Hkv*D*2; L2 flushed between steps when the "
                     "inputs are below 256 MB",
         "metric": "reshape_and_cache HBM GB/s", "unit": "GB/s", "points": sweep}
+    ex["reshape_sweep"]["cpu_baseline"] = cpu_reshape_sweep(R, sweep)
     del R
     torch.cuda.empty_cache()
     from tecoops import capi

@@ -5,7 +5,9 @@
 //     (99-165, same 14 positional arguments) — torch_ext.cpp:208-215;
 //   * rms_norm (81-97), the adjacent operator of the same decoder layer;
 //   * added: TORCH_LIBRARY(tecoops) ops
-//     torch.ops.tecoops.reshape_and_cache / torch.ops.tecoops.flash_attention.
+//     torch.ops.tecoops.reshape_and_cache / torch.ops.tecoops.flash_attention, and the
+//     one-launch decode step reshape_and_cache_flash_attn_decode /
+//     torch.ops.tecoops.reshape_and_cache_flash_attention_decode.
 // Differences from the reference binding (all B200-motivated):
 //   * q_seq_lens = diff(cu_seqlens_q) is computed ON THE DEVICE (the reference
 //     copies cu_seqlens_q to the host and back, a sync per call, 118-126);
@@ -195,6 +197,9 @@ static torch::Tensor run_flash(torch::Tensor q, torch::Tensor k, torch::Tensor v
     TORCH_CHECK(block_table.scalar_type() == at::kInt, "block_table must be int32");
     TORCH_CHECK(kv_lens.scalar_type() == at::kInt && q_lens.scalar_type() == at::kInt,
                 "sequence lengths must be int32");
+    TORCH_CHECK(q_lens.is_cuda() && kv_lens.is_cuda() && q_lens.get_device() == q.get_device() &&
+                    kv_lens.get_device() == q.get_device(),
+                "tecoops: sequence lengths must be CUDA tensors on q's device");
     if (!out.defined() || out.numel() == 0) out = torch::zeros_like(q);
     checkCuda(out, "out");
     c10::cuda::CUDAGuard g(q.device());
@@ -233,10 +238,12 @@ pybind11::object flash_attn_varlen_func_torch(torch::Tensor q, torch::Tensor k, 
     }
     const int64_t batch = seqused_k.size(0);
     TORCH_CHECK(cu_seqlens_q.numel() >= batch + 1, "cu_seqlens_q must hold batch + 1 offsets");
-    auto cu = cu_seqlens_q.to(at::kInt);
+    // offsets and lengths may come from the host (the reference binding copies them
+    // there itself): they are moved to q's device, without a host synchronisation
+    auto cu = cu_seqlens_q.to(q.device(), at::kInt);
     // per-sequence query lengths, computed on the device (no host round trip)
     auto q_lens = (cu.slice(0, 1, batch + 1) - cu.slice(0, 0, batch)).contiguous();
-    auto kv_lens = seqused_k.to(at::kInt).contiguous();
+    auto kv_lens = seqused_k.to(q.device(), at::kInt).contiguous();
     torch::Tensor lse;
     if (return_softmax_lse)
         lse = torch::full({q.size(1), q.size(0)}, -INFINITY, q.options().dtype(torch::kFloat));
@@ -244,6 +251,48 @@ pybind11::object flash_attn_varlen_func_torch(torch::Tensor q, torch::Tensor k, 
                        &opts, return_softmax_lse ? lse.data_ptr<float>() : nullptr);
     if (return_softmax_lse) return pybind11::make_tuple(o, lse);
     return pybind11::cast(o);
+}
+
+// One decode step in one launch (tecoopsReshapeAndCacheFlashAttentionDecode): the new
+// token of sequence b (row b of key / value, [B, Hkv, D]) is stored at cache slot
+// slot_mapping[b] (-1: skipped) and attended at position seqused_k[b] - 1 together with
+// the cached context; q / out [B, Hq, D].  Equals reshape_and_cache followed by
+// flash_attn_varlen_func with max_seqlen_q = 1 when slot_mapping[b] is the block-table slot
+// of that position.
+torch::Tensor reshape_and_cache_flash_attn_decode_torch(
+    torch::Tensor q, torch::Tensor key, torch::Tensor value, torch::Tensor k_cache,
+    torch::Tensor v_cache, torch::Tensor slot_mapping, torch::Tensor seqused_k,
+    torch::Tensor block_table, int64_t max_seqlen_k, torch::Tensor out) {
+    checkCuda(q, "q");
+    checkCuda(key, "key");
+    checkCuda(value, "value");
+    checkCuda(k_cache, "k_cache");
+    checkCuda(v_cache, "v_cache");
+    checkCuda(slot_mapping, "slot_mapping");
+    checkCuda(block_table, "block_table");
+    TORCH_CHECK(q.dim() == 3 && key.dim() == 3 && value.sizes() == key.sizes() &&
+                    key.size(0) == q.size(0),
+                "q [B, Hq, D] and key / value [B, Hkv, D] (one new token per sequence)");
+    TORCH_CHECK(slot_mapping.scalar_type() == at::kLong && slot_mapping.numel() >= q.size(0),
+                "slot_mapping must be int64 [B]");
+    TORCH_CHECK(block_table.scalar_type() == at::kInt, "block_table must be int32");
+    const int64_t batch = block_table.size(0);
+    TORCH_CHECK(seqused_k.numel() == batch, "seqused_k must be [B]");
+    auto kv_lens = seqused_k.to(q.device(), at::kInt).contiguous();
+    // every sequence has one query row: q_seq_lens = 1 (made on the device)
+    auto q_lens = torch::ones({batch}, kv_lens.options());
+    if (!out.defined() || out.numel() == 0) out = torch::zeros_like(q);
+    checkCuda(out, "out");
+    c10::cuda::CUDAGuard g(q.device());
+    tecoopsHandle_t h = handleFor(q.get_device());
+    Desc bt(block_table), qd(q), kd(k_cache), vd(v_cache), od(out);
+    checkStatus(tecoopsReshapeAndCacheFlashAttentionDecode(
+                    h, key.data_ptr(), value.data_ptr(), slot_mapping.data_ptr<int64_t>(),
+                    (int)max_seqlen_k, q_lens.data_ptr<int>(), kv_lens.data_ptr<int>(), bt.d,
+                    block_table.data_ptr(), qd.d, q.data_ptr(), kd.d, k_cache.data_ptr(), vd.d,
+                    v_cache.data_ptr(), od.d, out.data_ptr(), nullptr),
+                "tecoopsReshapeAndCacheFlashAttentionDecode");
+    return out;
 }
 
 // torch.ops.tecoops.* (C-API argument meaning: lengths, not offsets)
@@ -260,6 +309,15 @@ void flash_attention_op(const at::Tensor &q, const at::Tensor &k_cache,
     TORCH_CHECK(out.defined() && out.sizes() == q.sizes(), "out must have the shape of q");
     run_flash(q, k_cache, v_cache, q_seq_lens.contiguous(), kv_seq_lens.contiguous(),
               block_table, max_seqlen_q, max_seqlen_k, out);
+}
+
+void reshape_and_cache_flash_attention_decode_op(
+    const at::Tensor &q, const at::Tensor &key, const at::Tensor &value, at::Tensor k_cache,
+    at::Tensor v_cache, const at::Tensor &slot_mapping, const at::Tensor &kv_seq_lens,
+    const at::Tensor &block_table, int64_t max_seqlen_k, at::Tensor out) {
+    TORCH_CHECK(out.defined() && out.sizes() == q.sizes(), "out must have the shape of q");
+    reshape_and_cache_flash_attn_decode_torch(q, key, value, k_cache, v_cache, slot_mapping,
+                                              kv_seq_lens, block_table, max_seqlen_k, out);
 }
 
 void rms_norm_op(const at::Tensor &input, const at::Tensor &weight,
@@ -279,12 +337,18 @@ TORCH_LIBRARY(tecoops, m) {
         "flash_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor q_seq_lens, "
         "Tensor kv_seq_lens, Tensor block_table, int max_seqlen_q, int max_seqlen_k, "
         "Tensor(a!) out) -> ()");
+    m.def(
+        "reshape_and_cache_flash_attention_decode(Tensor q, Tensor key, Tensor value, "
+        "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor slot_mapping, Tensor kv_seq_lens, "
+        "Tensor block_table, int max_seqlen_k, Tensor(c!) out) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(tecoops, CUDA, m) {
     m.impl("reshape_and_cache", &reshape_and_cache_op);
     m.impl("flash_attention", &flash_attention_op);
     m.impl("rms_norm", &rms_norm_op);
+    m.impl("reshape_and_cache_flash_attention_decode",
+           &reshape_and_cache_flash_attention_decode_op);
 }
 
 PYBIND11_MODULE(_torch_ext, m) {
@@ -292,4 +356,6 @@ PYBIND11_MODULE(_torch_ext, m) {
     m.def("rms_norm", &rms_norm_torch, "rms_norm (sm_100a)");
     m.def("flash_attn_varlen_func", &flash_attn_varlen_func_torch,
           "flash_attn_varlen_func (sm_100a)");
+    m.def("reshape_and_cache_flash_attn_decode", &reshape_and_cache_flash_attn_decode_torch,
+          "one decode step: reshape_and_cache of the new tokens + attention (sm_100a)");
 }

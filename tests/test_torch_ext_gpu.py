@@ -153,3 +153,58 @@ def test_binding_two_streams_concurrently():
     for name, _, ref in runs:
         for it in range(5):
             assert torch.equal(outs[(name, it)], ref), (name, it)
+
+
+def test_host_offsets_and_lengths_are_accepted():
+    """cu_seqlens_q / seqused_k given as CPU tensors (the reference binding copies them to
+    the host itself): moved to q's device, same result as device tensors."""
+    import tecoops
+    from gpu_util import attn_case_to_dev
+    c = cases.ATTN_CASES["bf16_bs16_varlen"]
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    ql = inp["q_lens"]
+    cu = torch.zeros(len(ql) + 1, dtype=torch.int32)
+    cu[1:] = torch.from_numpy(np.cumsum(ql)).to(torch.int32)
+    outs = []
+    for dev in ("cuda", "cpu"):
+        outs.append(tecoops.flash_attn_varlen_func(
+            d["q"], d["kc"], d["vc"], int(ql.max()), cu.to(dev), int(inp["kv_lens"].max()),
+            torch.Tensor(), d["kv_lens"].to(dev), 0.0, True, torch.Tensor(), d["bt"], False,
+            torch.empty_like(d["q"])))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_fused_decode_step_binding():
+    """reshape_and_cache_flash_attn_decode (and its torch.ops form) equals
+    reshape_and_cache followed by flash_attn_varlen_func, caches and output bit-identical."""
+    import tecoops
+    from gpu_util import attn_case_to_dev
+    c = cases.ATTN_CASES["bf16_bs16_decode"]
+    inp = cases.attn_inputs(c)
+    d = attn_case_to_dev(inp, c["dtype"])
+    B, Hkv, D, bs = len(inp["q_lens"]), c["Hkv"], c["D"], c["bs"]
+    g = torch.Generator(device="cuda").manual_seed(77)
+    knew = torch.randn(B, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    vnew = torch.randn(B, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    kl = inp["kv_lens"]
+    slot = torch.tensor([int(inp["block_table"][b, (int(kl[b]) - 1) // bs]) * bs
+                         + (int(kl[b]) - 1) % bs for b in range(B)], device="cuda")
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    kc_a, vc_a = d["kc"].clone(), d["vc"].clone()
+    tecoops.reshape_and_cache(knew, vnew, slot, kc_a, vc_a)
+    ref = tecoops.flash_attn_varlen_func(d["q"], kc_a, vc_a, 1, cu, int(kl.max()), torch.Tensor(),
+                                         d["kv_lens"], 0.0, True, torch.Tensor(), d["bt"], False,
+                                         torch.empty_like(d["q"]))
+    kc_b, vc_b = d["kc"].clone(), d["vc"].clone()
+    out_b = tecoops.reshape_and_cache_flash_attn_decode(d["q"], knew, vnew, kc_b, vc_b, slot,
+                                                        d["kv_lens"], d["bt"], int(kl.max()),
+                                                        torch.empty_like(d["q"]))
+    kc_c, vc_c = d["kc"].clone(), d["vc"].clone()
+    out_c = torch.empty_like(d["q"])
+    torch.ops.tecoops.reshape_and_cache_flash_attention_decode(
+        d["q"], knew, vnew, kc_c, vc_c, slot, d["kv_lens"], d["bt"], int(kl.max()), out_c)
+    torch.cuda.synchronize()
+    for kc, vc, out in ((kc_b, vc_b, out_b), (kc_c, vc_c, out_c)):
+        assert torch.equal(kc, kc_a) and torch.equal(vc, vc_a) and torch.equal(out, ref)

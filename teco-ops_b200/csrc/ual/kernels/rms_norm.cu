@@ -133,10 +133,77 @@ __global__ void __launch_bounds__(256) rms_norm_warp_kernel(RmsNormArgs a) {
     row_norm<T, VPT, 32, RES>(a, row, threadIdx.x & 31);
 }
 
+// CTA per row, software-pipelined over the CTA's rows: the raw vectors of the next row
+// are loaded before this row's block-wide sum, so their DRAM latency overlaps the
+// reduction barrier and the stores instead of following them.
 template <typename T, int VPT, bool RES>
 __global__ void __launch_bounds__(256) rms_norm_cta_kernel(RmsNormArgs a) {
-    for (int row = blockIdx.x; row < a.num_tokens; row += gridDim.x)
-        row_norm<T, VPT, 256, RES>(a, row, threadIdx.x);
+    const int t = threadIdx.x;
+    const int D = a.hidden_size;
+    const int nvec = D >> 3;
+    __shared__ float part[8];
+    uint4 xr[VPT], rr[VPT];
+    auto load_row = [&](int row) {
+        const T *x = static_cast<const T *>(a.input) + (int64_t)row * a.stride;
+        const T *r = RES ? static_cast<const T *>(a.residual) + (int64_t)row * D : nullptr;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int v = t + i * 256;
+            if (v < nvec) {
+                xr[i] = ld_once16(x + v * 8);
+                if (RES) rr[i] = ld_once16(r + v * 8);
+            }
+        }
+    };
+    int row = blockIdx.x;
+    if (row < a.num_tokens) load_row(row);
+    for (; row < a.num_tokens; row += gridDim.x) {
+        float h[VPT][8];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            if (t + i * 256 < nvec) {
+                unpack8<T>(xr[i], h[i]);
+                if (RES) {
+                    float rf[8];
+                    unpack8<T>(rr[i], rf);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) h[i][e] += rf[e];
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss += h[i][e] * h[i][e];
+            }
+        }
+        const int next = row + (int)gridDim.x;
+        if (next < a.num_tokens) load_row(next);   // in flight during the sum and stores
+        ss = warp_sum(ss);
+        __syncthreads();   // the previous row's readers are done with `part`
+        if ((t & 31) == 0) part[t >> 5] = ss;
+        __syncthreads();
+        ss = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) ss += part[w];
+        const float rstd = 1.0f / sqrtf(ss / (float)D + a.eps);
+        T *y = static_cast<T *>(a.output) + (int64_t)row * D;
+        T *ro = RES ? static_cast<T *>(a.residual_out) + (int64_t)row * D : nullptr;
+        const uint4 *w = reinterpret_cast<const uint4 *>(a.weight);
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int v = t + i * 256;
+            if (v < nvec) {
+                float wf[8], o[8];
+                unpack8<T>(__ldg(w + v), wf);
+                if (RES) {
+                    const uint4 hp = pack8<T>(h[i]);
+                    *reinterpret_cast<uint4 *>(ro + v * 8) = hp;
+                    unpack8<T>(hp, h[i]);   // the output uses the rounded residual sum
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o[e] = h[i][e] * rstd * wf[e];
+                *reinterpret_cast<uint4 *>(y + v * 8) = pack8<T>(o);
+            }
+        }
+    }
 }
 
 // any hidden_size / alignment: two passes over global memory, CTA per row

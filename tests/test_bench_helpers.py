@@ -69,3 +69,50 @@ def test_verify_reference_matches_the_oracle():
                                    v.permute(1, 0, 2).numpy()[None], [S], [S],
                                    np.zeros((1, 1), dtype=np.int32))
     np.testing.assert_allclose(got.numpy(), ref[pos.numpy()], atol=2e-5, rtol=1e-5)
+
+
+def _fake_prefill_workload(lens, hq, hkv, seed=3):
+    """A CPU stand-in for bench.Llama8B with the attributes the CPU baseline reads."""
+    import types
+    g = torch.Generator().manual_seed(seed)
+    W = types.SimpleNamespace(lens=list(lens), tot=sum(lens), HKV=hkv, HQ=hq)
+    W.nb = sum(bench.cdiv(n, bench.BS) for n in lens)
+    W.q = torch.randn(W.tot, hq, bench.D, generator=g).to(torch.bfloat16)
+    W.k = torch.randn(W.tot, hkv, bench.D, generator=g).to(torch.bfloat16)
+    W.v = torch.randn(W.tot, hkv, bench.D, generator=g).to(torch.bfloat16)
+    bt = torch.zeros(len(lens), max(bench.cdiv(n, bench.BS) for n in lens), dtype=torch.int32)
+    slots, p0 = [], 0
+    for b, n in enumerate(lens):
+        pg = bench.cdiv(n, bench.BS)
+        bt[b, :pg] = torch.arange(p0, p0 + pg, dtype=torch.int32)
+        slots.append(torch.arange(n) + p0 * bench.BS)
+        p0 += pg
+    W.bt, W.slot = bt, torch.cat(slots)
+    W.flops = bench.attn_flops(lens, lens, hq=hq)
+    return W
+
+
+def test_cpu_baseline_of_the_prefill_runs_the_golden_on_the_same_inputs():
+    """bench's in-full CPU baseline (C reshape + the reference golden) on a small batch:
+    the GPU output it is compared with is here the oracle's, so the reported difference
+    is the golden-vs-oracle one, within the north-star tolerance."""
+    golden = bench._golden_or_none()
+    if golden is None:
+        pytest.skip("reference golden not installed (oracle/install_ref.py)")
+    W = _fake_prefill_workload([70, 33], hq=4, hkv=2)
+    kc = np.zeros((W.nb, 2, bench.BS, bench.D), np.uint16)
+    vc = np.zeros_like(kc)
+    oracle.reshape_and_cache(bench._words(W.k), bench._words(W.v), W.slot.numpy(), kc, vc)
+    f32 = lambda w: w.view(np.int16).astype(np.int32) << 16   # bf16 words -> fp32 bits
+    ref = oracle.flash_attn_varlen(W.q.float().numpy(), f32(kc).view(np.float32),
+                                   f32(vc).view(np.float32), W.lens, W.lens, W.bt.numpy())
+    W.out = torch.from_numpy(ref).to(torch.bfloat16)
+    r = bench.cpu_llama8b_prefill(W, golden)
+    assert r["kind"] == "reference" and r["unit"] == "TFLOP/s" and r["value"] > 0
+    assert r["gpu_vs_golden"]["max_abs"] <= 2e-2 and r["gpu_vs_golden"]["mean_abs"] <= 2e-3
+
+
+def test_median_of_runs():
+    calls = []
+    assert bench._median_s(lambda: calls.append(1), runs=3, warmup=2) >= 0
+    assert len(calls) == 5

@@ -158,7 +158,10 @@ FlashAttentionAlgos FlashAttentionOp::selectAlgo(const FlashAttentionArgs &a) {
     if (!aligned16(a.q) || !aligned16(a.fmha_out) || !aligned16(a.key_cache) ||
         !aligned16(a.value_cache) || !aligned16(a.new_key) || !aligned16(a.new_value))
         return FlashAttentionAlgos::GENERIC;
-    if (a.max_q_seq_len == 1 && kern::decode_supported(a.size_per_head, a.block_size, group))
+    // the split-KV grid is (splits, KV heads x head slices, sequences): its y and z
+    // extents are limited to 65,535
+    if (a.max_q_seq_len == 1 && kern::decode_supported(a.size_per_head, a.block_size, group) &&
+        a.batch_size <= 65535 && a.local_kv_head_num * ((group + 15) / 16) <= 65535)
         return FlashAttentionAlgos::DECODE_SPLITKV;
     // e4m3 caches reach the tcgen05 prefill through a dequantised compact copy
     if (kern::prefill_supported(a.size_per_head, a.block_size, group))

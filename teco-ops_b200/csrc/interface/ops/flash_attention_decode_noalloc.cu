@@ -143,10 +143,11 @@ extern "C" tecoopsStatus_t tecoopsFlashAttentionDecodeNoAlloc(
     const int batch = bt->dimA[0], heads = q->dimA[1], kv_heads = k->dimA[1];
     const int head_dim = q->dimA[2], block_size = k->dimA[2];
     const int group = heads / kv_heads;
-    if (!tecoops::kern::decode_supported(head_dim, block_size, group)) {
-        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: head_dim %d / block_size %d not covered "
-                   "by the split-KV decode kernel",
-                   head_dim, block_size);
+    if (!tecoops::kern::decode_supported(head_dim, block_size, group) || batch > 65535 ||
+        kv_heads * ((group + 15) / 16) > 65535) {
+        TECO_ERROR("tecoopsFlashAttentionDecodeNoAlloc: head_dim %d / block_size %d / batch %d "
+                   "not covered by the split-KV decode kernel",
+                   head_dim, block_size, batch);
         return TECOOPS_STATUS_NOT_SUPPORTED;
     }
     // decode precondition: at most one query row per sequence (every q_seq_lens[b] is 0

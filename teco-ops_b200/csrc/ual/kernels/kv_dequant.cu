@@ -44,9 +44,11 @@ __global__ void __launch_bounds__(256) kv_dequant_compact_kernel(KvDequantParams
     const int b = bi / p.pages_per_seq;
     const int i = bi - b * p.pages_per_seq;
     if (threadIdx.x == 0) p.bt_out[bi] = bi;
-    if (i * p.block_size >= __ldg(p.kv_seq_lens + b)) return;   // past kv_len: not read
+    // the length and the block-table entry are loaded together (one round trip)
+    const int kv_len = __ldg(p.kv_seq_lens + b);
     const int blk =
         i < p.block_table_dim ? __ldg(p.block_table + (int64_t)b * p.block_table_dim + i) : -1;
+    if (i * p.block_size >= kv_len) return;   // past kv_len: not read
     const bool valid = blk >= 0 && blk < p.num_pages;   // ids outside the pool give zeros
     const int dch = p.head_dim / 16;                    // 16-byte e4m3 chunks per row
     const int chunks = p.num_kv_heads * p.block_size * dch;   // per page, per cache

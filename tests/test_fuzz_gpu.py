@@ -4,7 +4,8 @@ The hand-picked parity cases follow the reference's tests; this sweep adds shape
 nobody picked: 1-6 sequences, query lengths 0..300 with kv lengths >= them (chunked
 prefill, empty sequences, kv lengths that end anywhere in a page or tile), GQA groups 1,
 2, 3, 4, 8, head_dim 64 / 128, block sizes 8..256, fp16 / bf16, shuffled page pools
-with spare pages, and decode calls (every q_len 0 or 1) through the split-KV branch.
+with spare pages, and decode calls (every q_len 0 or 1) through the split-KV branch; then
+the same shapes with random tecoopsFlashAttentionEx options and random cache formats.
 Every case must meet the north-star tolerance (max-abs <= 2e-2, mean-abs <= 2e-3)."""
 import numpy as np
 import pytest
@@ -99,3 +100,59 @@ def test_random_options_match_the_oracle(i):
     if fin.any():
         err = np.abs(lse[fin] - rlse[fin]).max()
         assert err <= LSE_ABS, (c, err)
+
+
+@pytest.mark.parametrize("i", range(24))
+def test_random_cache_formats_match_the_oracle(i):
+    """The sweep's shapes on the cache formats beyond the reference: the vLLM page layout
+    [NB, bs, Hkv, D] and e4m3 caches with per-tensor scales (tecoopsFlashAttentionEx),
+    against the oracle on the dequantised cache (16-bit vLLM layout: bit-identical to the
+    reference layout instead)."""
+    from gpu_util import attention_capi, attn_case_to_dev, errors, handle, words_to_dev
+    from oracle import fp8
+    from tecoops import capi
+    c = _case(200 + i)
+    rng = np.random.default_rng(8000 + i)
+    layout = int(rng.integers(0, 2))
+    e4m3 = bool(rng.integers(0, 2)) or layout == 0
+    inp = cases.attn_inputs(c)
+    dt = capi.DATA_HALF if c["dtype"] == "f16" else capi.DATA_BFLOAT16
+    q = words_to_dev(inp["q"], c["dtype"])
+    ql = torch.from_numpy(inp["q_lens"]).cuda()
+    kl = torch.from_numpy(inp["kv_lens"]).cuda()
+    bt = torch.from_numpy(inp["block_table"]).cuda()
+    perm = (lambda a: np.ascontiguousarray(a.transpose(0, 2, 1, 3))) if layout else (lambda a: a)
+    if e4m3:
+        ks, vs = float(rng.choice([1 / 64, 1 / 16, 0.5])), float(rng.choice([1 / 32, 0.25]))
+        kq = fp8.quantize(seeded.words_to_f32(inp["k_cache"], c["dtype"]), ks)
+        vq = fp8.quantize(seeded.words_to_f32(inp["v_cache"], c["dtype"]), vs)
+        kd, vd = torch.from_numpy(perm(kq)).cuda(), torch.from_numpy(perm(vq)).cuda()
+        cdt = capi.DATA_FLOAT8_E4M3
+    else:
+        ks = vs = 1.0
+        kd = words_to_dev(perm(inp["k_cache"]), c["dtype"])
+        vd = words_to_dev(perm(inp["v_cache"]), c["dtype"])
+        cdt = dt
+    out = torch.full_like(q, 3.0)
+    dq, dc = capi.Desc(dt, q.shape), capi.Desc(cdt, kd.shape)
+    st = capi.flash_attention_ex(handle(), int(inp["q_lens"].max()), int(inp["kv_lens"].max()),
+                                 kd.shape[0], ql.data_ptr(), kl.data_ptr(),
+                                 capi.Desc(capi.DATA_INT32, bt.shape), bt.data_ptr(), dq,
+                                 q.data_ptr(), dc, kd.data_ptr(), dc, vd.data_ptr(), dq,
+                                 out.data_ptr(), 0, kv_layout=layout, k_scale=ks, v_scale=vs)
+    capi.check(st, "tecoopsFlashAttentionEx")
+    torch.cuda.synchronize()
+    if not e4m3:
+        d = attn_case_to_dev(inp, c["dtype"])
+        ref = attention_capi(d["q"], d["kc"], d["vc"], d["q_lens"], d["kv_lens"], d["bt"],
+                             out=torch.full_like(d["q"], 3.0))
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), c
+        return
+    ref = oracle.flash_attn_varlen(seeded.words_to_f32(inp["q"], c["dtype"]),
+                                   fp8.dequantize(kq, ks), fp8.dequantize(vq, vs),
+                                   inp["q_lens"], inp["kv_lens"], inp["block_table"])
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all(), c
+    mx, mean, _ = errors(got, ref)
+    assert mx <= 2e-2 and mean <= 2e-3, (c, layout, ks, vs, mx, mean)

@@ -5,7 +5,8 @@ nobody picked: 1-6 sequences, query lengths 0..300 with kv lengths >= them (chun
 prefill, empty sequences, kv lengths that end anywhere in a page or tile), GQA groups 1,
 2, 3, 4, 8, head_dim 64 / 128, block sizes 8..256, fp16 / bf16, shuffled page pools
 with spare pages, and decode calls (every q_len 0 or 1) through the split-KV branch; then
-the same shapes with random tecoopsFlashAttentionEx options and random cache formats.
+the same shapes with random tecoopsFlashAttentionEx options and random cache formats;
+and random reshape_and_cache cases, bit-exact.
 Every case must meet the north-star tolerance (max-abs <= 2e-2, mean-abs <= 2e-3)."""
 import numpy as np
 import pytest
@@ -156,3 +157,32 @@ def test_random_cache_formats_match_the_oracle(i):
     assert np.isfinite(got).all(), c
     mx, mean, _ = errors(got, ref)
     assert mx <= 2e-2 and mean <= 2e-3, (c, layout, ks, vs, mx, mean)
+
+
+def _reshape_case(i):
+    rng = np.random.default_rng(9500 + i)
+    bs = int(rng.choice([8, 16, 32, 128]))
+    NB = int(rng.integers(4, 200))
+    T = int(rng.integers(1, min(NB * bs, 5000) + 1))
+    return dict(T=T, H=int(rng.choice([1, 2, 4, 8])), D=int(rng.choice([64, 72, 128, 256])),
+                NB=NB, bs=bs, dtype=str(rng.choice(["f16", "bf16"])),
+                slots=str(rng.choice(["perm", "arange"])),
+                pad=float(rng.choice([0.0, 0.1, 0.5])), init="random", seed=900 + i)
+
+
+@pytest.mark.parametrize("i", range(24))
+def test_random_reshape_is_bit_exact(i):
+    """tecoopsReshapeAndCache on random token counts, head counts, head sizes (including a
+    non-multiple of 8: the scalar path), block sizes, padding fractions and distinct slots,
+    into caches holding earlier data: every word equal to the oracle's, untouched slots
+    kept."""
+    from gpu_util import dev_to_words, reshape_capi, words_to_dev
+    c = _reshape_case(i)
+    key, value, slot, kc, vc = cases.reshape_inputs(c)
+    ek, ev = oracle.reshape_and_cache(key, value, slot, kc.copy(), vc.copy())
+    dk, dv = words_to_dev(kc, c["dtype"]), words_to_dev(vc, c["dtype"])
+    reshape_capi(words_to_dev(key, c["dtype"]), words_to_dev(value, c["dtype"]),
+                 torch.from_numpy(slot).cuda(), dk, dv)
+    torch.cuda.synchronize()
+    assert np.array_equal(dev_to_words(dk), ek), c
+    assert np.array_equal(dev_to_words(dv), ev), c

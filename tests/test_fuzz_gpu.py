@@ -6,7 +6,7 @@ prefill, empty sequences, kv lengths that end anywhere in a page or tile), GQA g
 2, 3, 4, 8, head_dim 64 / 128, block sizes 8..256, fp16 / bf16, shuffled page pools
 with spare pages, and decode calls (every q_len 0 or 1) through the split-KV branch; then
 the same shapes with random tecoopsFlashAttentionEx options and random cache formats;
-and random reshape_and_cache cases, bit-exact.
+random reshape_and_cache cases, bit-exact; and random rms_norm cases.
 Every case must meet the north-star tolerance (max-abs <= 2e-2, mean-abs <= 2e-3)."""
 import numpy as np
 import pytest
@@ -186,3 +186,37 @@ def test_random_reshape_is_bit_exact(i):
     torch.cuda.synchronize()
     assert np.array_equal(dev_to_words(dk), ek), c
     assert np.array_equal(dev_to_words(dv), ev), c
+
+
+@pytest.mark.parametrize("i", range(16))
+def test_random_rms_norm_matches_the_oracle(i):
+    """rms_norm (with and without the residual add) on random token counts and hidden sizes
+    (warp-per-row, CTA-per-row and scalar paths), fp16 / bf16: residual_out bit-exact, the
+    output within one step of the 16-bit type of the oracle."""
+    from gpu_util import handle, words_to_dev, dev_to_words
+    from tecoops import capi
+    rng = np.random.default_rng(9700 + i)
+    hidden = int(rng.choice([64, 100, 128, 1000, 2048, 2056, 4096, 5120, 8192, 16384]))
+    c = cases._rn(int(rng.integers(1, 700)), hidden, float(rng.choice([1e-6, 1e-5])),
+                  bool(rng.integers(0, 2)), seed=700 + i, dtype=str(rng.choice(["f16", "bf16"])),
+                  dist=str(rng.choice(["uniform", "normal"])))
+    x, w, r = cases.rms_inputs(c)
+    dx, dw = words_to_dev(x, c["dtype"]), words_to_dev(w, c["dtype"])
+    dr = words_to_dev(r, c["dtype"]) if r is not None else None
+    out = torch.empty_like(dx)
+    ro = torch.empty_like(dx) if r is not None else None
+    capi.check(capi.rms_norm(handle(), dx.data_ptr(), dw.data_ptr(),
+                             dr.data_ptr() if dr is not None else 0, out.data_ptr(),
+                             ro.data_ptr() if ro is not None else 0, c["N"], c["D"], c["eps"],
+                             dtype=None if c["dtype"] == "f16" else capi.DATA_BFLOAT16),
+               "tecoopsRmsNorm")
+    torch.cuda.synchronize()
+    ey, ero = oracle.rms_norm(x, w, r, c["eps"], c["dtype"])
+    yo = seeded.words_to_f32(dev_to_words(out), c["dtype"])
+    ye = seeded.words_to_f32(ey, c["dtype"])
+    mant = 10 if c["dtype"] == "f16" else 7
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ye), np.float32(2.0 ** -14)))) - mant)
+    assert np.isfinite(yo).all(), c
+    assert np.all(np.abs(yo - ye) <= ulp + 1e-7), (c, np.abs(yo - ye).max())
+    if r is not None:
+        assert np.array_equal(dev_to_words(ro), ero), c

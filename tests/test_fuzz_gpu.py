@@ -6,7 +6,8 @@ prefill, empty sequences, kv lengths that end anywhere in a page or tile), GQA g
 2, 3, 4, 8, head_dim 64 / 128, block sizes 8..256, fp16 / bf16, shuffled page pools
 with spare pages, and decode calls (every q_len 0 or 1) through the split-KV branch; then
 the same shapes with random tecoopsFlashAttentionEx options and random cache formats;
-random reshape_and_cache cases, bit-exact; and random rms_norm cases.
+random reshape_and_cache cases, bit-exact; random rms_norm cases; and random fused decode
+steps against the two operators.
 Every case must meet the north-star tolerance (max-abs <= 2e-2, mean-abs <= 2e-3)."""
 import numpy as np
 import pytest
@@ -220,3 +221,60 @@ def test_random_rms_norm_matches_the_oracle(i):
     assert np.all(np.abs(yo - ye) <= ulp + 1e-7), (c, np.abs(yo - ye).max())
     if r is not None:
         assert np.array_equal(dev_to_words(ro), ero), c
+
+
+@pytest.mark.parametrize("i", range(16))
+def test_random_fused_decode_step_equals_two_operators(i):
+    """tecoopsReshapeAndCacheFlashAttentionDecode on random decode shapes (GQA groups
+    1-16, head_dim 64 / 128, block sizes 16-128, contexts 1-3,000, padding sequences with
+    slot -1): output and caches bit-identical to tecoopsReshapeAndCache followed by
+    tecoopsFlashAttention."""
+    from gpu_util import attention_capi, handle, reshape_capi
+    from tecoops import capi
+    rng = np.random.default_rng(9900 + i)
+    B = int(rng.integers(1, 40))
+    Hkv = int(rng.choice([1, 2, 8]))
+    group = int(rng.choice([1, 2, 4, 8, 16]))
+    D = int(rng.choice([64, 128]))
+    bs = int(rng.choice([16, 32, 64, 128]))
+    dt = torch.float16 if rng.integers(0, 2) else torch.bfloat16
+    ctx = [int(x) for x in rng.integers(1, 3001, B)]   # kv_len including the new token
+    pages = [(c + bs - 1) // bs for c in ctx]
+    pool = sum(pages) + int(rng.integers(0, 9))
+    perm = torch.from_numpy(rng.permutation(pool).astype(np.int32))
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    p0 = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[p0:p0 + pages[b]]
+        p0 += pages[b]
+    g = torch.Generator(device="cuda").manual_seed(9900 + i)
+    kc = torch.randn(pool, Hkv, bs, D, device="cuda", generator=g).to(dt)
+    vc = torch.randn(pool, Hkv, bs, D, device="cuda", generator=g).to(dt)
+    q = torch.randn(B, Hkv * group, D, device="cuda", generator=g).to(dt)
+    kn = torch.randn(B, Hkv, D, device="cuda", generator=g).to(dt)
+    vn = torch.randn(B, Hkv, D, device="cuda", generator=g).to(dt)
+    slot = [int(bt[b, (ctx[b] - 1) // bs]) * bs + (ctx[b] - 1) % bs for b in range(B)]
+    for b in range(B):
+        if rng.random() < 0.1:
+            slot[b] = -1
+    slot = torch.tensor(slot, dtype=torch.int64, device="cuda")
+    ones = torch.ones(B, dtype=torch.int32, device="cuda")
+    kv = torch.tensor(ctx, dtype=torch.int32, device="cuda")
+    btd = bt.cuda()
+    kc_a, vc_a = kc.clone(), vc.clone()
+    reshape_capi(kn, vn, slot, kc_a, vc_a)
+    ref = attention_capi(q, kc_a, vc_a, ones, kv, btd, max_q=1, max_k=max(ctx))
+    kc_b, vc_b = kc.clone(), vc.clone()
+    out = torch.zeros_like(q)
+    cdt = capi.DATA_HALF if dt == torch.float16 else capi.DATA_BFLOAT16
+    dq, dc = capi.Desc(cdt, q.shape), capi.Desc(cdt, kc.shape)
+    capi.check(capi.reshape_and_cache_flash_attention_decode(
+        handle(), kn.data_ptr(), vn.data_ptr(), slot.data_ptr(), max(ctx), ones.data_ptr(),
+        kv.data_ptr(), capi.Desc(capi.DATA_INT32, bt.shape), btd.data_ptr(), dq, q.data_ptr(),
+        dc, kc_b.data_ptr(), dc, vc_b.data_ptr(), dq, out.data_ptr()), "fused decode")
+    torch.cuda.synchronize()
+    assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b), (B, Hkv, group, D, bs)
+    # a padding sequence (slot -1) attends its stale cached row in the two-operator form and
+    # the new row in the fused one (which takes the new token from the inputs)
+    keep = (slot >= 0).cpu()
+    assert torch.equal(out[keep], ref[keep]), (B, Hkv, group, D, bs)
